@@ -1,0 +1,399 @@
+"""Benchmark of the B200 MoE hot path (one JSON line on rank 0).
+
+Default workload (every N): configuration 2 - one Top-2 MoE layer, d_model
+256, 16 experts, d_ff 1024, 512 packed samples with lengths U{16..256}
+(T = 69,632 tokens for seed 0), bf16 activations and experts, fp32 router,
+Zipf(1.2) expert bias.  A step is one SMoE forward over the whole packed
+batch.  With N GPUs every rank runs its own replica on its own batch (the
+layer does not shard at this size), so scaling is weak.
+
+value  tokens/s of the whole job, inputs resident in HBM, device time from
+       CUDA events (max over ranks), L2 flushed between steps.
+e2e    the same through the public API with host buffers: pinned host x ->
+       device, SMoE.forward, output -> pinned host, all inside the timed
+       region.
+roofline  the dominant kernel (the expert FFN GEMM) timed alone with CUDA
+       events: algorithmic FLOPs / mean launch time vs the measured bf16 peak.
+cpu_baseline  the reference's PyTorch CPU expert loop (oracle port of
+       baseline/infer.py:280-358, fp32) on a bounded token sample, rank 0,
+       N=1 only.
+
+--impl reference times that CPU implementation alone on the same workload
+(rank 0 only; other ranks exit without work).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+CPU_SAMPLE_TOKENS = 8192
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """Samples nvidia-smi every 200 ms while the timed region runs and keeps
+    the rows of this process's GPU (matched by UUID)."""
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.file = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid).replace("GPU-", "")
+        except Exception:
+            self.uuid = ""
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader", "-lms",
+                 "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.file.read())) if len(r) >= 9]
+        os.unlink(self.file.name)
+        mine = [r for r in rows if self.uuid and self.uuid in r[0]]
+        rows = mine or rows
+        sm, smax, reasons = [], [], set()
+        for r in rows:
+            try:
+                sm.append(float(r[1].strip().split()[0]))
+                smax.append(float(r[2].strip().split()[0]))
+            except (ValueError, IndexError):
+                continue
+            for name, v in zip(self.REASONS, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm), "matched_uuid": bool(mine)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the oracle port of the reference's expert loop)
+# ---------------------------------------------------------------------------
+def cpu_baseline_moe(cfg, seconds: float, sample_tokens: int = CPU_SAMPLE_TOKENS):
+    from cti_b200 import synth
+    from oracle import moe_ref as mr
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    T, _ = synth.moe_tokens(cfg)
+    S = min(sample_tokens, T)
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias)
+    x = synth.moe_activations(T, cfg.d_model)[:S].float()
+    w1, w2 = w.w1.float(), w.w2.float()
+    with torch.no_grad():
+        mr.smoe_ref(x, w.wg, w.bg, w1, w.b1, w2, w.b2)  # warm-up
+        n = 0
+        t0 = time.perf_counter()
+        while True:
+            mr.smoe_ref(x, w.wg, w.bg, w1, w.b1, w2, w.b2)
+            n += 1
+            el = time.perf_counter() - t0
+            if (el >= seconds and n >= 2) or n >= 10000:
+                break
+    return {"value": n * S / el, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{S} of the {T} configuration-2 tokens per call, {n} calls "
+                      f"({el:.1f} s), fp32, oracle/moe_ref.py (baseline/infer.py:280-358)"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU expert loop (oracle port) on rank 0."""
+    if rank != 0:
+        return
+    from cti_b200 import synth
+    from oracle import moe_ref as mr
+
+    cfg = synth.CFG2
+    torch.set_num_threads(os.cpu_count() or 1)
+    T, _ = synth.moe_tokens(cfg)
+    S = min(CPU_SAMPLE_TOKENS, T)
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias)
+    x = synth.moe_activations(T, cfg.d_model)[:S].float()
+    w1, w2 = w.w1.float(), w.w2.float()
+    times = []
+    with torch.no_grad():
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            mr.smoe_ref(x, w.wg, w.bg, w1, w.b1, w2, w.b2)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+    step = statistics.mean(times)
+    value = S / step
+    line = {
+        "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": value,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cfg, T, sample=S),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{S} of {T} tokens per step (oracle/moe_ref.py, the "
+                                   f"reference's fp32 expert loop)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(cfg, T, sample=None):
+    c = {"workload": f"{cfg.name}: Top-2 MoE layer, d_model {cfg.d_model}, {cfg.num_experts} "
+                     f"experts, d_ff {cfg.dim_ff}, {cfg.samples} packed samples U{{16..256}}",
+         "tokens": T, "d_model": cfg.d_model, "experts": cfg.num_experts, "d_ff": cfg.dim_ff,
+         "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
+         "l2": "flushed (256 MiB write) before every timed step", "per_gpu": "one replica"}
+    if sample is not None:
+        c["cpu_sample_tokens"] = sample
+    return c
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def time_steps(fn, steps, flush, dev):
+    """Per-step device time (ms) of fn(), L2 flushed before each step outside
+    the event pair."""
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        times.append((s, e))
+    torch.cuda.synchronize(dev)
+    return [s.elapsed_time(e) for s, e in times]
+
+
+def stage_times(m, x2, flush, dev, reps=10):
+    """Mean device time (ms) of each stage launched separately."""
+    from cti_b200 import ops
+
+    names = ["router", "dispatch", "ffn_fc1", "ffn_fc2", "combine"]
+    acc = {n: [] for n in names}
+    for _ in range(reps):
+        flush.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        ev[0].record()
+        r = ops.router(x2, m._wg, m._bg, renorm=True)
+        ev[1].record()
+        d = ops.dispatch(x2, r, m.num_experts)
+        ev[2].record()
+        h = ops.grouped_gemm(d.xperm, m._w1, m._b1, d.offsets, act="gelu")
+        ev[3].record()
+        y = ops.grouped_gemm(h, m._w2, m._b2, d.offsets, act="none")
+        ev[4].record()
+        ops.combine(y, d.perm_inv, r.gate2)
+        ev[5].record()
+        torch.cuda.synchronize(dev)
+        for i, n in enumerate(names):
+            acc[n].append(ev[i].elapsed_time(ev[i + 1]))
+    return {n: statistics.mean(v) for n, v in acc.items()}
+
+
+def run_ours(args, world, rank, local):
+    import cti_b200
+    from cti_b200 import _lib, synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = synth.CFG2
+    T, cu = synth.moe_tokens(cfg, seed=0)
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, seed=0,
+                          device=dev)
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts).to(dev)
+    synth.load_moe_module(m, w)
+    m.prepare_for_inference()
+    x = synth.moe_activations(T, cfg.d_model, seed=rank, device=dev)
+    x3 = x.unsqueeze(0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    for _ in range(args.warmup):
+        m(x3)
+    torch.cuda.synchronize(dev)
+    _lib.raise_on_status(dev)
+
+    sampler = ClockSampler(dev) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.start()
+    times = time_steps(lambda: m(x3), args.steps, flush, dev)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    _lib.raise_on_status(dev)
+    step_ms = max_over_ranks(statistics.mean(times), world, dev)
+    tokens_all = sum_over_ranks(float(T), world, dev)
+    value = tokens_all / (step_ms / 1e3)
+
+    # End to end through the public API with host buffers.
+    x_h = x.cpu().pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+    x_d = torch.empty_like(x)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        out, _ = m(x_d.unsqueeze(0))
+        out_h.copy_(out[0], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e2e_times = time_steps(e2e_step, args.steps, flush, dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+    e2e_value = tokens_all / (e2e_ms / 1e3)
+
+    stages = stage_times(m, x, flush, dev)
+    peaks, peak_src = load_peaks()
+    R = 2 * T
+    ffn_flops = 2.0 * R * cfg.d_model * cfg.dim_ff  # one of the two expert GEMMs
+    dom = "ffn_fc1" if stages["ffn_fc1"] >= stages["ffn_fc2"] else "ffn_fc2"
+    achieved = ffn_flops / (stages[dom] / 1e3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    launches_per_step = 6
+
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_moe(cfg, args.cpu_seconds)
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(cfg, T),
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": x_h.numel() * x_h.element_size(),
+                "d2h_bytes_per_step": out_h.numel() * out_h.element_size()},
+        "roofline": {"bound": "tensor", "kernel": f"grouped_gemm ({dom})",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": f"bf16_tflops of {peak_src}",
+                     "flops_per_launch": ffn_flops, "traffic": None},
+        "layer_roofline_frac": (2 * ffn_flops / (step_ms / 1e3) / 1e12 / world) / peak,
+        "stages_ms": stages,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")),
+                      int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+// Library-level entry points: identity, device query, status words, and
+// the one-call MoE layer (router -> dispatch -> expert FFN -> combine) that
+// mirrors SMoE.forward (online_best/infer.py:1910-1954) for C callers.
+#include <cstring>
+
+#include "common.cuh"
+#include "tmap.cuh"
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+inline size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+// Workspace carve-up of cti_moe_layer_forward; the same function sizes it
+// (base == nullptr) and places the buffers.
+struct LayerWorkspace {
+  int32_t* idx2;
+  float* gate2;
+  int32_t* rank;
+  int32_t* hist;
+  int32_t* offsets;
+  int32_t* perm_inv;
+  int32_t* sorted_token;
+  void* xperm;
+  void* hidden;
+  void* y;
+  size_t bytes;
+
+  LayerWorkspace(void* base, int64_t T, int D, int E, int F) {
+    auto* p = static_cast<uint8_t*>(base);
+    size_t off = 0;
+    auto take = [&](size_t n) -> void* {
+      void* r = p ? p + off : nullptr;
+      off += align_up(n);
+      return r;
+    };
+    const int64_t R = 2 * T;
+    idx2 = static_cast<int32_t*>(take(sizeof(int32_t) * R));
+    gate2 = static_cast<float*>(take(sizeof(float) * R));
+    rank = static_cast<int32_t*>(take(sizeof(int32_t) * R));
+    hist = static_cast<int32_t*>(take(cti_moe_dispatch_workspace_bytes(T, E)));
+    offsets = static_cast<int32_t*>(take(sizeof(int32_t) * (E + 1)));
+    perm_inv = static_cast<int32_t*>(take(sizeof(int32_t) * R));
+    sorted_token = static_cast<int32_t*>(take(sizeof(int32_t) * R));
+    xperm = take((size_t)2 * R * D);
+    hidden = take((size_t)2 * R * F);
+    y = take((size_t)2 * R * D);
+    bytes = off;
+  }
+};
+
+}  // namespace
+
+extern "C" const char* cti_version(void) { return "cti_b200 0.1.0 sm_100a"; }
+
+extern "C" int cti_num_sms(int device, int* num_sms) {
+  if (!num_sms) return CTI_ERR_INVALID_ARG;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return CTI_ERR_CUDA;
+  *num_sms = n;
+  return CTI_OK;
+}
+
+extern "C" int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail,
+                               void* stream) {
+  if (!status) return CTI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t host[2] = {0, 0};
+  if (cudaMemcpyAsync(host, status, sizeof(host), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return CTI_ERR_CUDA;
+  if (clear && cudaMemsetAsync(status, 0, sizeof(host), s) != cudaSuccess) return CTI_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return CTI_ERR_CUDA;
+  if (code) *code = host[0];
+  if (detail) *detail = host[1];
+  return CTI_OK;
+}
+
+extern "C" size_t cti_moe_layer_workspace_bytes(int64_t T, int D, int E, int F) {
+  if (T < 0 || D <= 0 || E <= 0 || F <= 0) return 0;
+  return LayerWorkspace(nullptr, T, D, E, F).bytes;
+}
+
+extern "C" int cti_moe_layer_forward(const void* x_bf16, const float* wg, const float* bg,
+                                     const void* W1_bf16, const float* b1, const void* W2_bf16,
+                                     const float* b2, int64_t T, int D, int E, int F, int act,
+                                     int renorm, void* out_bf16, void* workspace,
+                                     size_t workspace_bytes, int32_t* status, void* stream) {
+  if (T < 0 || D <= 0 || E < 2 || F <= 0) return CTI_ERR_INVALID_ARG;
+  if (T == 0) return CTI_OK;
+  if (!workspace || workspace_bytes < cti_moe_layer_workspace_bytes(T, D, E, F))
+    return CTI_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0) return CTI_ERR_INVALID_ARG;
+  LayerWorkspace ws(workspace, T, D, E, F);
+  const int64_t R = 2 * T;
+  int rc = cti_moe_router(x_bf16, wg, bg, T, D, E, renorm, ws.idx2, ws.gate2, ws.rank, ws.hist,
+                          status, stream);
+  if (rc) return rc;
+  rc = cti_moe_dispatch(x_bf16, ws.idx2, ws.rank, ws.hist, T, D, E, ws.offsets, ws.perm_inv,
+                        ws.sorted_token, ws.xperm, status, stream);
+  if (rc) return rc;
+  rc = cti_moe_expert_ffn_fused(ws.xperm, W1_bf16, b1, W2_bf16, b2, ws.offsets, E, E, R, D, F,
+                                act, ws.y, status, stream);
+  if (rc == CTI_ERR_UNSUPPORTED) {
+    rc = cti_moe_grouped_gemm(ws.xperm, W1_bf16, b1, ws.offsets, E, E, R, F, D, act, ws.hidden,
+                              status, stream);
+    if (rc) return rc;
+    rc = cti_moe_grouped_gemm(ws.hidden, W2_bf16, b2, ws.offsets, E, E, R, D, F, CTI_ACT_NONE,
+                              ws.y, status, stream);
+  }
+  if (rc) return rc;
+  return cti_moe_combine(ws.y, R, ws.perm_inv, ws.gate2, T, D, out_bf16, status, stream);
+}

@@ -1,0 +1,219 @@
+// Stage 2 (dispatch) and stage 4 (combine).
+//
+// Dispatch restates the reference's per-expert grouping of routes
+// (baseline/infer.py:336-346: for each expert, `mask.nonzero()` in token
+// order, then `x_flat[token_idx]`; online_best/infer.py:1205-1290 count /
+// prefix / pack kernels) as a deterministic counting sort:
+//   1. dispatch_scan_kernel: one CTA turns the router's per-block expert
+//      histograms into expert offsets[E+1] and per-block base offsets (an
+//      exclusive prefix over blocks, then over experts).
+//   2. dispatch_scatter_kernel: one warp per token computes the sorted
+//      position of its two routes (block base + in-block rank from the
+//      router) and copies the token row to both positions with 16-byte
+//      vector loads/stores.
+// Routes of one expert come out in token order, exactly the order of the
+// reference's `nonzero()`.
+//
+// Combine restates `out_flat[token_idx] += expert_out * weight`
+// (baseline/infer.py:350-353) and moe_top2_reduce_kernel
+// (online_best/infer.py:1603-1621): one warp per token reads the token's two
+// expert-output rows, weights them by the gates in fp32 and writes one bf16
+// row.
+#include "common.cuh"
+
+namespace cti {
+namespace {
+
+constexpr int kScanThreads = 1024;
+
+// hist: [nblk, E] per-block expert counts; rewritten in place into
+// per-block base positions.  offsets: [E+1].
+__global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __restrict__ hist,
+                                                                    int64_t nblk, int E,
+                                                                    int32_t* __restrict__ offsets) {
+  __shared__ int32_t part[kScanThreads];
+  __shared__ int32_t total[CTI_MAX_EXPERTS];
+  __shared__ int32_t base[CTI_MAX_EXPERTS + 1];
+  const int tid = threadIdx.x;
+  const int chunks = kScanThreads / E;  // block-chunks per expert
+  const int64_t per = (nblk + chunks - 1) / chunks;
+  const int e = tid % E;
+  const int c = tid / E;
+  const bool active = c < chunks;
+  const int64_t b_lo = active ? c * per : 0;
+  const int64_t b_hi = active ? min(nblk, b_lo + per) : 0;
+
+  int32_t sum = 0;
+  for (int64_t b = b_lo; b < b_hi; ++b) sum += hist[b * E + e];
+  part[tid] = sum;
+  __syncthreads();
+  if (tid < E) {
+    int32_t run = 0;
+    for (int cc = 0; cc < chunks; ++cc) {
+      const int32_t v = part[cc * E + tid];
+      part[cc * E + tid] = run;
+      run += v;
+    }
+    total[tid] = run;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int32_t run = 0;
+    for (int ee = 0; ee < E; ++ee) {
+      base[ee] = run;
+      run += total[ee];
+    }
+    base[E] = run;
+  }
+  __syncthreads();
+  if (tid <= E) offsets[tid] = base[tid];
+  if (active) {
+    int32_t run = base[e] + part[tid];
+    for (int64_t b = b_lo; b < b_hi; ++b) {
+      const int32_t v = hist[b * E + e];
+      hist[b * E + e] = run;
+      run += v;
+    }
+  }
+}
+
+// One warp per token.  D % 8 == 0 (16-byte chunks of 8 bf16).
+__global__ void __launch_bounds__(256) dispatch_scatter_kernel(
+    const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx2,
+    const int32_t* __restrict__ route_rank, const int32_t* __restrict__ block_base, int64_t T,
+    int D, int E, int32_t* __restrict__ perm_inv, int32_t* __restrict__ sorted_token,
+    __nv_bfloat16* __restrict__ xperm, int32_t* status) {
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int64_t R = 2 * T;
+  const int2 e = reinterpret_cast<const int2*>(idx2)[t];
+  const int2 rk = reinterpret_cast<const int2*>(route_rank)[t];
+  const int64_t blk = t / CTI_ROUTER_BLOCK_TOKENS;
+  if (e.x < 0 || e.x >= E || e.y < 0 || e.y >= E) {
+    if (lane == 0) raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
+    return;
+  }
+  const int64_t p0 = (int64_t)block_base[blk * E + e.x] + rk.x;
+  const int64_t p1 = (int64_t)block_base[blk * E + e.y] + rk.y;
+  if (p0 < 0 || p0 >= R || p1 < 0 || p1 >= R) {
+    if (lane == 0) raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
+    return;
+  }
+  if (lane == 0) {
+    reinterpret_cast<int2*>(perm_inv)[t] = make_int2((int)p0, (int)p1);
+    sorted_token[p0] = (int32_t)t;
+    sorted_token[p1] = (int32_t)t;
+  }
+  if (xperm == nullptr) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
+  uint4* d0 = reinterpret_cast<uint4*>(xperm + p0 * D);
+  uint4* d1 = reinterpret_cast<uint4*>(xperm + p1 * D);
+  const int nchunk = D / 8;
+  for (int c = lane; c < nchunk; c += 32) {
+    const uint4 v = __ldg(src + c);
+    d0[c] = v;
+    d1[c] = v;
+  }
+}
+
+// One warp per token.
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ Y,
+                                                     int64_t Y_rows,
+                                                     const int32_t* __restrict__ perm_inv,
+                                                     const float* __restrict__ gate2, int64_t T,
+                                                     int D, __nv_bfloat16* __restrict__ out,
+                                                     int32_t* status) {
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int2 p = reinterpret_cast<const int2*>(perm_inv)[t];
+  const float2 g = reinterpret_cast<const float2*>(gate2)[t];
+  if (p.x < 0 || p.x >= Y_rows || p.y < 0 || p.y >= Y_rows) {
+    if (lane == 0) raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
+    return;
+  }
+  const uint4* y0 = reinterpret_cast<const uint4*>(Y + (int64_t)p.x * D);
+  const uint4* y1 = reinterpret_cast<const uint4*>(Y + (int64_t)p.y * D);
+  uint4* o = reinterpret_cast<uint4*>(out + t * D);
+  const int nchunk = D / 8;
+  for (int c = lane; c < nchunk; c += 32) {
+    const uint4 a = __ldg(y0 + c);
+    const uint4 b = __ldg(y1 + c);
+    const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
+    uint4 r;
+    uint32_t* rw = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fa = __bfloat1622float2(ha[j]);
+      const float2 fb = __bfloat1622float2(hb[j]);
+      rw[j] = pack_bf16x2(fmaf(g.y, fb.x, g.x * fa.x), fmaf(g.y, fb.y, g.x * fa.y));
+    }
+    o[c] = r;
+  }
+}
+
+inline bool misaligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0;
+}
+
+}  // namespace
+}  // namespace cti
+
+extern "C" size_t cti_moe_dispatch_workspace_bytes(int64_t T, int E) {
+  if (T <= 0 || E <= 0) return 0;
+  const int64_t nblk = (T + CTI_ROUTER_BLOCK_TOKENS - 1) / CTI_ROUTER_BLOCK_TOKENS;
+  return (size_t)nblk * (size_t)E * sizeof(int32_t);
+}
+
+extern "C" int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const int32_t* route_rank,
+                                int32_t* block_hist, int64_t T, int D, int E, int32_t* offsets,
+                                int32_t* perm_inv, int32_t* sorted_token, void* xperm_bf16,
+                                int32_t* status, void* stream) {
+  using namespace cti;
+  if (T < 0 || D <= 0 || E < 2 || E > CTI_MAX_EXPERTS) return CTI_ERR_INVALID_ARG;
+  if (D % 8 != 0) return CTI_ERR_UNSUPPORTED;
+  if (2 * T > INT32_MAX) return CTI_ERR_UNSUPPORTED;
+  if (!offsets) return CTI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    // No routes: every expert segment is empty.
+    return cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), s) == cudaSuccess
+               ? CTI_OK
+               : CTI_ERR_CUDA;
+  }
+  if (!idx2 || !route_rank || !block_hist || !perm_inv || !sorted_token)
+    return CTI_ERR_INVALID_ARG;
+  if (xperm_bf16 && (!x_bf16 || misaligned(x_bf16, 16) || misaligned(xperm_bf16, 16)))
+    return CTI_ERR_INVALID_ARG;
+  if (misaligned(idx2, 8) || misaligned(route_rank, 8) || misaligned(perm_inv, 8))
+    return CTI_ERR_INVALID_ARG;
+  const int64_t nblk = (T + CTI_ROUTER_BLOCK_TOKENS - 1) / CTI_ROUTER_BLOCK_TOKENS;
+  dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(block_hist, nblk, E, offsets);
+  if (cudaGetLastError() != cudaSuccess) return CTI_ERR_CUDA;
+  const int64_t blocks = (T + 7) / 8;
+  dispatch_scatter_kernel<<<(unsigned)blocks, 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x_bf16), idx2, route_rank, block_hist, T, D, E, perm_inv,
+      sorted_token, static_cast<__nv_bfloat16*>(xperm_bf16), status);
+  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+}
+
+extern "C" int cti_moe_combine(const void* Y_bf16, int64_t Y_rows, const int32_t* perm_inv,
+                               const float* gate2, int64_t T, int D, void* out_bf16,
+                               int32_t* status, void* stream) {
+  using namespace cti;
+  if (T < 0 || D <= 0 || Y_rows < 0) return CTI_ERR_INVALID_ARG;
+  if (D % 8 != 0) return CTI_ERR_UNSUPPORTED;
+  if (T == 0) return CTI_OK;
+  if (!Y_bf16 || !perm_inv || !gate2 || !out_bf16) return CTI_ERR_INVALID_ARG;
+  if (misaligned(Y_bf16, 16) || misaligned(out_bf16, 16) || misaligned(perm_inv, 8) ||
+      misaligned(gate2, 8))
+    return CTI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t blocks = (T + 7) / 8;
+  combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(Y_bf16),
+                                                  Y_rows, perm_inv, gate2, T, D,
+                                                  static_cast<__nv_bfloat16*>(out_bf16), status);
+  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+}

@@ -1,0 +1,203 @@
+"""Tensor-level wrappers of the five hot-path stages.
+
+Each function validates its tensors, passes raw device pointers and the
+current CUDA stream to one ``libcti_b200.so`` entry point, and returns torch
+tensors.  They are the building blocks of :class:`SMoE` and
+:class:`RepEncoder`, and what the parity tests drive stage by stage.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, require_cuda, stream_handle, status_word
+
+
+@dataclass
+class RouterOut:
+    idx2: torch.Tensor  # [T, 2] int32 expert ids (top-1, top-2)
+    gate2: torch.Tensor  # [T, 2] fp32 gate weights
+    route_rank: torch.Tensor  # [T, 2] int32 rank inside the 128-token block
+    block_hist: torch.Tensor  # [ceil(T/128), E] int32 per-block expert counts
+
+
+@dataclass
+class DispatchOut:
+    offsets: torch.Tensor  # [E+1] int32 expert segment starts
+    perm_inv: torch.Tensor  # [T, 2] int32 sorted position of each route
+    sorted_token: torch.Tensor  # [2T] int32 token of each sorted row
+    xperm: torch.Tensor | None  # [2T, D] bf16 rows in expert order
+
+
+def router(x: torch.Tensor, wg: torch.Tensor, bg: torch.Tensor, renorm: bool = True) -> RouterOut:
+    """Stage 1: fp32 Top-2 router (see cti_moe_router)."""
+    require_cuda(x, "x", torch.bfloat16)
+    require_cuda(wg, "wg", torch.float32)
+    require_cuda(bg, "bg", torch.float32)
+    T, D = x.shape
+    E = wg.shape[0]
+    dev = x.device
+    nblk = (T + _lib.ROUTER_BLOCK_TOKENS - 1) // _lib.ROUTER_BLOCK_TOKENS
+    idx2 = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    gate2 = torch.empty((T, 2), dtype=torch.float32, device=dev)
+    rank = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    hist = torch.empty((max(nblk, 1), E), dtype=torch.int32, device=dev)
+    check(
+        lib.cti_moe_router(
+            ptr(x), ptr(wg), ptr(bg), T, D, E, int(renorm), ptr(idx2), ptr(gate2), ptr(rank),
+            ptr(hist), ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_moe_router",
+    )
+    return RouterOut(idx2, gate2, rank, hist)
+
+
+def dispatch(x: torch.Tensor, r: RouterOut, num_experts: int, permute: bool = True) -> DispatchOut:
+    """Stage 2: offsets + stable permutation of rows into expert order.
+
+    Consumes ``r.block_hist`` (rewritten in place into per-block bases)."""
+    require_cuda(x, "x", torch.bfloat16)
+    T, D = x.shape
+    dev = x.device
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    perm_inv = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    sorted_token = torch.empty(2 * T, dtype=torch.int32, device=dev)
+    xperm = torch.empty((2 * T, D), dtype=torch.bfloat16, device=dev) if permute else None
+    check(
+        lib.cti_moe_dispatch(
+            ptr(x), ptr(r.idx2), ptr(r.route_rank), ptr(r.block_hist), T, D, num_experts,
+            ptr(offsets), ptr(perm_inv), ptr(sorted_token), ptr(xperm),
+            ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_moe_dispatch",
+    )
+    return DispatchOut(offsets, perm_inv, sorted_token, xperm)
+
+
+def grouped_gemm(
+    a: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor | None,
+    group_offsets: torch.Tensor,
+    act: str = "none",
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Stage 3: C = act(A[group rows] @ W[g % Gw]^T + bias[g % Gw]).
+
+    a [rows, K] bf16; w [Gw, N, K] bf16; bias [Gw, N] fp32 or None;
+    group_offsets [G+1] int32 on the device."""
+    require_cuda(a, "A", torch.bfloat16)
+    require_cuda(w, "W", torch.bfloat16)
+    require_cuda(group_offsets, "group_offsets", torch.int32)
+    if bias is not None:
+        require_cuda(bias, "bias", torch.float32)
+    rows, K = a.shape
+    Gw, N, K2 = w.shape
+    if K2 != K:
+        raise ValueError(f"K mismatch: A has {K}, W has {K2}")
+    G = group_offsets.numel() - 1
+    dev = a.device
+    if out is None:
+        out = torch.empty((rows, N), dtype=torch.bfloat16, device=dev)
+    check(
+        lib.cti_moe_grouped_gemm(
+            ptr(a), ptr(w), ptr(bias), ptr(group_offsets), G, Gw, rows, N, K,
+            _lib.ACTIVATIONS[act], ptr(out), ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_moe_grouped_gemm",
+    )
+    return out
+
+
+def expert_ffn_fused(
+    xp: torch.Tensor,
+    w1: torch.Tensor,
+    b1: torch.Tensor,
+    w2: torch.Tensor,
+    b2: torch.Tensor,
+    group_offsets: torch.Tensor,
+    act: str = "gelu",
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Stage 3, fused: Y = act(Xp @ W1[e]^T + b1[e]) @ W2[e]^T + b2[e] per group."""
+    require_cuda(xp, "Xp", torch.bfloat16)
+    require_cuda(w1, "W1", torch.bfloat16)
+    require_cuda(w2, "W2", torch.bfloat16)
+    require_cuda(b1, "b1", torch.float32)
+    require_cuda(b2, "b2", torch.float32)
+    rows, D = xp.shape
+    Gw, F, _ = w1.shape
+    G = group_offsets.numel() - 1
+    dev = xp.device
+    if out is None:
+        out = torch.empty((rows, D), dtype=torch.bfloat16, device=dev)
+    check(
+        lib.cti_moe_expert_ffn_fused(
+            ptr(xp), ptr(w1), ptr(b1), ptr(w2), ptr(b2), ptr(group_offsets), G, Gw, rows, D, F,
+            _lib.ACTIVATIONS[act], ptr(out), ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_moe_expert_ffn_fused",
+    )
+    return out
+
+
+def combine(y: torch.Tensor, perm_inv: torch.Tensor, gate2: torch.Tensor,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Stage 4: out[t] = g0*Y[perm_inv[t,0]] + g1*Y[perm_inv[t,1]] (fp32 math, bf16 out)."""
+    require_cuda(y, "Y", torch.bfloat16)
+    require_cuda(perm_inv, "perm_inv", torch.int32)
+    require_cuda(gate2, "gate2", torch.float32)
+    T = perm_inv.shape[0]
+    D = y.shape[1]
+    dev = y.device
+    if out is None:
+        out = torch.empty((T, D), dtype=torch.bfloat16, device=dev)
+    check(
+        lib.cti_moe_combine(
+            ptr(y), y.shape[0], ptr(perm_inv), ptr(gate2), T, D, ptr(out),
+            ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_moe_combine",
+    )
+    return out
+
+
+def embedding_bag_sum(
+    values: torch.Tensor,
+    row_offsets: torch.Tensor,
+    val_offsets: torch.Tensor,
+    table: torch.Tensor,
+    table_row_base: torch.Tensor,
+    vocab: torch.Tensor,
+    num_features: int,
+    out_dtype: torch.dtype = torch.float32,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Stage 5: pooled[b, f*dim:(f+1)*dim] = sum of clamped table rows of bag (b, f).
+
+    The reference's flat layout: values int64 [N]; row_offsets int64
+    [F*(B+1)] per-feature offsets; val_offsets int64 [F]."""
+    for name, t in (("values", values), ("row_offsets", row_offsets),
+                    ("val_offsets", val_offsets), ("table_row_base", table_row_base),
+                    ("vocab", vocab)):
+        require_cuda(t, name, torch.int64)
+    require_cuda(table, "table", torch.float16)
+    F = num_features
+    if row_offsets.numel() % F != 0:
+        raise ValueError("row_offsets length must be a multiple of the feature count")
+    B = row_offsets.numel() // F - 1
+    dim = table.shape[1]
+    dev = table.device
+    if out is None:
+        out = torch.empty((B, F * dim), dtype=out_dtype, device=dev)
+    check(
+        lib.cti_embbag_sum(
+            ptr(values), values.numel(), ptr(row_offsets), ptr(val_offsets),
+            ptr(table_row_base), ptr(vocab), ptr(table), table.shape[0], B, F, dim, ptr(out),
+            _lib.DTYPE_CODES[out.dtype], ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_embbag_sum",
+    )
+    return out

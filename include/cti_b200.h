@@ -1,0 +1,185 @@
+/*
+ * cti_b200.h - C ABI of the B200 (sm_100a) hot path of the generative
+ * ad-ranking CTR model: the Top-2 sparse MoE layer and the 28-feature
+ * embedding-bag pooling that feeds it.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are raw device pointers to contiguous row-major
+ *     buffers that the caller owns (for example torch tensors); sizes are
+ *     element counts.  bf16/fp16 buffers are passed as `void*`.
+ *   - `stream` is a cudaStream_t passed as `void*`; all work is enqueued on
+ *     it, nothing synchronises the host, and no entry point allocates device
+ *     memory.  Scratch needs are met by caller-provided workspaces whose sizes
+ *     the *_workspace_bytes queries return.
+ *   - The return value is CTI_OK or a CTI_ERR_* code describing a host-side
+ *     argument or launch problem.  Problems that only the device can see (an
+ *     index outside a buffer, a bounded wait that ran out) are written to the
+ *     caller's device status word `status` (int32[2]: code, detail) and the
+ *     offending element is skipped; read it with cti_status_read.
+ *   - There is no fallback path: an unsupported shape is an error.
+ */
+#ifndef CTI_B200_H_
+#define CTI_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return / status codes. */
+#define CTI_OK 0
+#define CTI_ERR_INVALID_ARG 1  /* null pointer, bad size, misaligned buffer */
+#define CTI_ERR_UNSUPPORTED 2  /* shape outside what the kernels implement   */
+#define CTI_ERR_CUDA 3         /* a CUDA runtime/driver call failed           */
+#define CTI_ERR_TIMEOUT 4      /* device: a bounded wait ran out              */
+#define CTI_ERR_BOUNDS 5       /* device: an index pointed outside a buffer   */
+
+/* Expert activations (fc1 epilogue). */
+#define CTI_ACT_NONE 0
+#define CTI_ACT_RELU 1 /* reference model: baseline/infer.py:287            */
+#define CTI_ACT_GELU 2 /* exact-erf GELU of the benchmark configurations    */
+
+/* Output dtypes of the embedding-bag pooling. */
+#define CTI_DTYPE_F32 0
+#define CTI_DTYPE_BF16 1
+#define CTI_DTYPE_F16 2
+
+/* Tokens handled by one router block; the dispatch scratch holds one
+ * E-wide histogram per block. */
+#define CTI_ROUTER_BLOCK_TOKENS 128
+#define CTI_MAX_EXPERTS 128
+
+/* Library identity and device query. */
+const char* cti_version(void);
+int cti_num_sms(int device, int* num_sms);
+
+/* Reads (and optionally clears) a device status word int32[2] on `stream`;
+ * synchronises that stream. */
+int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 1 - router.
+ * Replaces TopKGate.forward (baseline/infer.py:298-309; online_best/infer.py:
+ * 1800-1852) and the fused_top2_gate_kernel launch (online_best/infer.py:
+ * 1624-1778, launched at :1818 and :2210).
+ *
+ * logits[t,e] = bg[e] + sum_d x[t,d]*wg[e,d] in fp32 (x is bf16, wg/bg fp32);
+ * the sum is one fused-multiply-add chain in increasing d.  Top-2 by logit
+ * with ties to the lower expert id.  renorm=1: gates are the two softmax
+ * probabilities renormalised to sum to 1; renorm=0: the raw softmax
+ * probabilities (the reference's un-renormalised scores).
+ * Outputs: idx2[T,2] int32, gate2[T,2] fp32, route_rank[T,2] int32 (rank of
+ * each route among the same-expert routes of its 128-token block, token
+ * order), block_hist[ceil(T/128), E] int32 (per-block expert counts; the
+ * dispatch scratch).  E <= 128.
+ * ---------------------------------------------------------------------- */
+int cti_moe_router(const void* x_bf16, const float* wg, const float* bg, int64_t T, int D, int E,
+                   int renorm, int32_t* idx2, float* gate2, int32_t* route_rank,
+                   int32_t* block_hist, int32_t* status, void* stream);
+
+/* Bytes of dispatch scratch (block_hist) for T tokens and E experts. */
+size_t cti_moe_dispatch_workspace_bytes(int64_t T, int E);
+
+/* ------------------------------------------------------------------------
+ * Stage 2 - dispatch.
+ * Replaces moe_route_count_kernel / moe_prefix8_kernel /
+ * moe_route_pack(_chunked)_kernel and SMoE._pack_routes*
+ * (online_best/infer.py:1205-1290, :1987-2062) and the per-expert
+ * `mask.nonzero()` + `x_flat[token_idx]` gather of baseline/infer.py:336-346.
+ *
+ * Turns block_hist (from cti_moe_router, rewritten in place into per-block
+ * base offsets) into expert offsets[E+1] (int32, exclusive prefix), then
+ * places every route r=(t,k) at position pos = offsets[e] + (number of
+ * earlier routes to e in token order): perm_inv[t,k] = pos,
+ * sorted_token[pos] = t, xperm[pos,:] = x[t,:].  Deterministic.
+ * xperm may be NULL (positions only; used by expert parallelism).
+ * ---------------------------------------------------------------------- */
+int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const int32_t* route_rank,
+                     int32_t* block_hist, int64_t T, int D, int E, int32_t* offsets,
+                     int32_t* perm_inv, int32_t* sorted_token, void* xperm_bf16, int32_t* status,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 3 - grouped expert GEMM on tcgen05 tensor cores.
+ * Replaces moe_sparse_fc1*_kernel and moe_sparse_fc2*_kernel
+ * (online_best/infer.py:1293-1600) and Expert.forward (baseline/infer.py:
+ * 286-287).
+ *
+ * For every group g (rows group_offsets[g] .. group_offsets[g+1]-1 of A):
+ *   C[rows, :] = act(A[rows, :K] @ W[g % Gw]^T + bias[g % Gw])
+ * A [rows_total, K] bf16, W [Gw, N, K] bf16 (the nn.Linear weight layout,
+ * stacked), bias [Gw, N] fp32 (may be NULL), C [rows_total, N] bf16.
+ * group_offsets is a device int32[G+1] array (non-decreasing, starting at 0);
+ * rows_total bounds it.  N % 128 == 0, K % 64 == 0, G <= 1024.
+ * ---------------------------------------------------------------------- */
+int cti_moe_grouped_gemm(const void* A_bf16, const void* W_bf16, const float* bias,
+                         const int32_t* group_offsets, int G, int Gw, int64_t rows_total, int N,
+                         int K, int act, void* C_bf16, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 3 (fused) - expert FFN with the hidden activation kept on chip.
+ * Y[rows,:] = (act(Xp[rows,:] @ W1[e]^T + b1[e])) @ W2[e]^T + b2[e]
+ * for e = g % Gw; the [rows, F] hidden tile never leaves the SM.
+ * Xp [rows_total, D], W1 [Gw, F, D], b1 [Gw, F] fp32, W2 [Gw, D, F],
+ * b2 [Gw, D] fp32, Y [rows_total, D] bf16.  D in {128, 256}; F % 128 == 0.
+ * Replaces the fc1 -> packed_hidden -> fc2 round trip of
+ * SMoE._chunked_compute (online_best/infer.py:2109-2173).
+ * ---------------------------------------------------------------------- */
+int cti_moe_expert_ffn_fused(const void* Xp_bf16, const void* W1_bf16, const float* b1,
+                             const void* W2_bf16, const float* b2, const int32_t* group_offsets,
+                             int G, int Gw, int64_t rows_total, int D, int F, int act,
+                             void* Y_bf16, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 4 - gate-weighted combine.
+ * Replaces moe_top2_reduce_kernel (online_best/infer.py:1603-1621), the
+ * `* score` of the fc2 epilogue (:1465-1473) and the
+ * `out_flat[token_idx] += expert_out * weight` of baseline/infer.py:350-353.
+ * out[t,:] = bf16( gate2[t,0]*Y[perm_inv[t,0],:] + gate2[t,1]*Y[perm_inv[t,1],:] )
+ * in fp32.  Y has Y_rows rows (bounds-checked).
+ * ---------------------------------------------------------------------- */
+int cti_moe_combine(const void* Y_bf16, int64_t Y_rows, const int32_t* perm_inv,
+                    const float* gate2, int64_t T, int D, void* out_bf16, int32_t* status,
+                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * Whole layer: router -> dispatch -> expert FFN -> combine, one call.
+ * The drop-in for SMoE.forward (online_best/infer.py:1910-1954; baseline/
+ * infer.py:323-358) for a caller that binds only C.
+ * wg/bg fp32 [E,D]/[E]; W1 [E,F,D], b1 [E,F] fp32, W2 [E,D,F], b2 [E,D]
+ * fp32; x/out [T,D] bf16.  workspace: cti_moe_layer_workspace_bytes bytes.
+ * ---------------------------------------------------------------------- */
+size_t cti_moe_layer_workspace_bytes(int64_t T, int D, int E, int F);
+int cti_moe_layer_forward(const void* x_bf16, const float* wg, const float* bg,
+                          const void* W1_bf16, const float* b1, const void* W2_bf16,
+                          const float* b2, int64_t T, int D, int E, int F, int act, int renorm,
+                          void* out_bf16, void* workspace, size_t workspace_bytes,
+                          int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 5 - 28-feature embedding-bag sum pooling.
+ * Replaces fused_all_slots_embedding_kernel and its launch
+ * (online_best/infer.py:793-827, :1029-1059) and the per-slot
+ * `emb(values.clamp(0, V-1))` + `segment_reduce(sum)` loop of
+ * RepEncoder.forward (baseline/infer.py:253-263).
+ *
+ * Flat layout of the reference batch: values int64 [n_values]; row_offsets
+ * int64 [F*(B+1)] (per-feature offsets, each feature's block starting at 0);
+ * val_offsets int64 [F] (start of each feature's values).  Tables are rows
+ * of one fp16 [total_rows, dim] buffer: feature f uses rows
+ * table_row_base[f] .. table_row_base[f] + vocab[f] - 1 and clamps ids to
+ * [0, vocab[f]-1].  out[b, f*dim + c] = sum over the bag in order, fp32
+ * accumulation, stored as out_dtype.  dim in {32, 64, 128, 256, 512}.
+ * ---------------------------------------------------------------------- */
+int cti_embbag_sum(const int64_t* values, int64_t n_values, const int64_t* row_offsets,
+                   const int64_t* val_offsets, const int64_t* table_row_base,
+                   const int64_t* vocab, const void* table_f16, int64_t table_rows, int64_t B,
+                   int F, int dim, void* out, int out_dtype, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CTI_B200_H_ */

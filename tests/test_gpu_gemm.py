@@ -1,0 +1,90 @@
+"""Stage 3 grouped GEMM (tcgen05/TMEM/TMA) on the B200 vs a torch fp32
+reference of the same op.  Tolerance: max rel err 8e-3 (the bf16 rounding of
+the output is 2^-9 relative; fp32 accumulation order differences are far
+below it)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from helpers import max_rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 8e-3
+
+
+def ref_grouped(a, w, bias, offs, act, Gw):
+    out = torch.zeros(a.shape[0], w.shape[1])
+    o = offs.tolist()
+    for g in range(len(o) - 1):
+        lo, hi = o[g], o[g + 1]
+        if hi <= lo:
+            continue
+        gw = g % Gw
+        v = a[lo:hi].float() @ w[gw].float().T
+        if bias is not None:
+            v = v + bias[gw]
+        if act == "gelu":
+            v = F.gelu(v)
+        elif act == "relu":
+            v = F.relu(v)
+        out[lo:hi] = v
+    return out
+
+
+CASES = [
+    # rows, K, N, group sizes, Gw, act
+    (128, 64, 128, [128], 1, "none"),
+    (128, 128, 256, [128], 1, "none"),
+    (300, 128, 128, [0, 130, 170], 3, "relu"),
+    (2000, 256, 1024, [250, 0, 700, 1, 127, 129, 300, 493], 8, "gelu"),
+    (2048, 1024, 256, [1000, 24, 1024], 3, "none"),
+    (1500, 256, 512, [200, 300, 100, 400, 250, 250], 3, "gelu"),
+    (40000, 256, 256, [20000, 15000, 5000], 3, "none"),
+]
+
+
+@pytest.mark.parametrize("rows,K,N,sizes,Gw,act", CASES)
+def test_grouped_gemm_matches_fp32(cuda_device, rows, K, N, sizes, Gw, act):
+    from cti_b200 import _lib, ops
+
+    assert sum(sizes) == rows
+    g = torch.Generator().manual_seed(rows + K + N)
+    a = torch.randn(rows, K, generator=g).bfloat16()
+    w = (torch.randn(Gw, N, K, generator=g) * 0.05).bfloat16()
+    bias = torch.randn(Gw, N, generator=g) * 0.1
+    offs = torch.zeros(len(sizes) + 1, dtype=torch.int32)
+    offs[1:] = torch.cumsum(torch.tensor(sizes), 0)
+    dev = cuda_device
+    out = ops.grouped_gemm(a.to(dev), w.to(dev), bias.to(dev), offs.to(dev), act=act)
+    _lib.raise_on_status(dev)
+    ref = ref_grouped(a, w, bias, offs, act, Gw)
+    err = max_rel_err(out, ref)
+    assert err < TOL, f"max rel err {err}"
+
+
+def test_grouped_gemm_leaves_rows_outside_groups_untouched(cuda_device):
+    from cti_b200 import _lib, ops
+
+    dev = cuda_device
+    rows, K, N = 500, 128, 128
+    a = torch.randn(rows, K, device=dev).bfloat16()
+    w = (torch.randn(1, N, K, device=dev) * 0.05).bfloat16()
+    offs = torch.tensor([0, 300], dtype=torch.int32, device=dev)
+    out = torch.full((rows, N), 7.0, device=dev).bfloat16()
+    ops.grouped_gemm(a, w, None, offs, out=out)
+    _lib.raise_on_status(dev)
+    assert (out[300:] == 7.0).all()
+    ref = a[:300].float() @ w[0].float().T
+    assert max_rel_err(out[:300], ref) < TOL
+
+
+def test_grouped_gemm_reports_bad_offsets(cuda_device):
+    from cti_b200 import _lib, ops
+
+    dev = cuda_device
+    a = torch.randn(256, 64, device=dev).bfloat16()
+    w = torch.randn(1, 128, 64, device=dev).bfloat16()
+    offs = torch.tensor([0, 300], dtype=torch.int32, device=dev)  # the group runs past A
+    ops.grouped_gemm(a, w, None, offs)
+    code, detail = _lib.read_status(dev)
+    assert code == _lib.CTI_ERR_BOUNDS and detail == 0

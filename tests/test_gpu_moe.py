@@ -1,0 +1,156 @@
+"""The whole MoE layer on the B200 (SMoE.forward through cti_moe_layer_forward)
+vs the reference: fixtures made by the reference's own code, and the CPU
+oracle at the benchmark shapes.  Tolerance: max rel err 2e-2 (bf16 kernels
+vs the fp32 reference; helpers.max_rel_err); expert indices bit-exact outside
+the fp64 near-tie band."""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+from helpers import MOE_MAX_REL_ERR, load_golden, max_rel_err
+from oracle import moe_ref as mr
+
+pytestmark = pytest.mark.gpu
+
+
+def build_module(inp, D, E, Fd, dev):
+    import cti_b200
+
+    m = cti_b200.SMoE(D, Fd, E, activation=inp["act"], renormalize=inp["renorm"])
+    with torch.no_grad():
+        m.gate.w_g.weight.copy_(inp["wg"])
+        m.gate.w_g.bias.copy_(inp["bg"])
+        for e, ex in enumerate(m.experts):
+            ex.fc1.weight.copy_(inp["w1"][e])
+            ex.fc1.bias.copy_(inp["b1"][e])
+            ex.fc2.weight.copy_(inp["w2"][e])
+            ex.fc2.bias.copy_(inp["b2"][e])
+    m.to(dev)
+    m.prepare_for_inference()
+    return m
+
+
+@pytest.mark.parametrize("name", list(gi.MOE_CASES))
+def test_smoe_matches_reference_fixture(cuda_device, name):
+    from cti_b200 import _lib
+
+    D, E, Fd, T, act, renorm, _ = gi.MOE_CASES[name]
+    inp = gi.moe_inputs(name)
+    gold = load_golden(name)
+    m = build_module(inp, D, E, Fd, cuda_device)
+    x = inp["x"].bfloat16().to(cuda_device).unsqueeze(0)
+    out, aux = m(x)
+    _lib.raise_on_status(cuda_device)
+    assert aux is None and out.shape == (1, T, D) and out.dtype == torch.bfloat16
+    err = max_rel_err(out[0], torch.from_numpy(gold["out"]))
+    assert err < MOE_MAX_REL_ERR, err
+    idx, score = m.gate(x)
+    np.testing.assert_array_equal(idx[0].cpu().numpy(), gold["idx"])
+    np.testing.assert_allclose(score[0].cpu().numpy(), gold["score"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("cfg_name", ["cfg1", "cfg2"])
+@pytest.mark.parametrize("fused", [False, None])
+def test_smoe_matches_oracle_at_benchmark_shape(cuda_device, cfg_name, fused):
+    from cti_b200 import _lib, synth
+
+    cfg = synth.MOE_CONFIGS[cfg_name]
+    T, _ = synth.moe_tokens(cfg)
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias)
+    x = synth.moe_activations(T, cfg.d_model)
+    import cti_b200
+
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device).prepare_for_inference()
+    xd = x.to(cuda_device)
+    if fused is False:
+        out = m.forward_staged(xd, fused=False)["out"]
+    else:
+        out = m(xd.unsqueeze(0))[0][0]
+    _lib.raise_on_status(cuda_device)
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref, g = mr.smoe_ref(x.float(), w.wg, w.bg, w.w1.float(), w.b1, w.w2.float(), w.b2)
+    err = max_rel_err(out, ref)
+    assert err < MOE_MAX_REL_ERR, err
+    tie = mr.near_tie_mask(x.float(), w.wg, w.bg)
+    idx, _ = m.gate(xd.unsqueeze(0))
+    ok = ~tie
+    assert torch.equal(idx[0].cpu()[ok], g.idx[ok])
+
+
+def test_smoe_stages_agree_with_layer_call(cuda_device):
+    from cti_b200 import _lib, synth
+    import cti_b200
+
+    cfg = synth.CFG2
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, seed=3)
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device).prepare_for_inference()
+    x = synth.moe_activations(9000, cfg.d_model, seed=3).to(cuda_device)
+    st = m.forward_staged(x, fused=False)
+    out = m(x.unsqueeze(0))[0][0]
+    _lib.raise_on_status(cuda_device)
+    assert torch.equal(out, st["out"]) or max_rel_err(out, st["out"]) < 8e-3
+
+
+@pytest.mark.parametrize("T", [1, 2, 255, 256, 257])
+def test_smoe_small_token_counts(cuda_device, T):
+    """The reference switches paths at T < 256 (online_best/infer.py:2077,
+    :2196); here every T takes the same kernels."""
+    from cti_b200 import _lib, synth
+    import cti_b200
+
+    w = synth.moe_weights(128, 8, 512, None, seed=T)
+    m = cti_b200.SMoE(128, 512, 8)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device).prepare_for_inference()
+    x = synth.moe_activations(T, 128, seed=T)
+    out = m(x.to(cuda_device).unsqueeze(0))[0][0]
+    _lib.raise_on_status(cuda_device)
+    ref, _ = mr.smoe_ref(x.float(), w.wg, w.bg, w.w1.float(), w.b1, w.w2.float(), w.b2)
+    assert max_rel_err(out, ref) < MOE_MAX_REL_ERR
+
+
+def test_smoe_empty_input(cuda_device):
+    import cti_b200
+
+    m = cti_b200.SMoE(128, 256, 8).to(cuda_device)
+    out, _ = m(torch.zeros(1, 0, 128, dtype=torch.bfloat16, device=cuda_device))
+    assert out.shape == (1, 0, 128)
+
+
+def test_output_does_not_alias_input_and_residual_add_works(cuda_device):
+    """The caller does torch.add(moe_out, residual, out=residual)
+    (online_best/infer.py:2513)."""
+    from cti_b200 import synth
+    import cti_b200
+
+    w = synth.moe_weights(256, 16, 1024, 1.2)
+    m = cti_b200.SMoE(256, 1024, 16)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device)
+    x = synth.moe_activations(1000, 256).to(cuda_device).unsqueeze(0)
+    residual = x.clone()
+    out, _ = m(x)
+    assert out.data_ptr() != x.data_ptr()
+    expect = out.float() + residual.float()
+    torch.add(out, residual, out=residual)
+    assert max_rel_err(residual, expect) < 1e-2
+
+
+def test_expert_forward_runs_on_the_grouped_gemm(cuda_device):
+    from cti_b200 import _lib, synth
+    import cti_b200
+
+    w = synth.moe_weights(128, 8, 512, None)
+    m = cti_b200.SMoE(128, 512, 8)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device)
+    x = synth.moe_activations(300, 128).to(cuda_device)
+    y = m.experts[2](x)
+    _lib.raise_on_status(cuda_device)
+    ref = mr.expert_ref(x.float().cpu(), w.w1[2].float(), w.b1[2], w.w2[2].float(), w.b2[2], "gelu")
+    assert max_rel_err(y, ref) < 1e-2

@@ -1,0 +1,87 @@
+"""Host-side logic: module API parity with the reference, synthetic inputs.  No GPU."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cti_b200
+from cti_b200 import synth
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def test_state_dict_keys_match_reference():
+    ref_keys = (GOLDEN / "reference_state_dict_keys.txt").read_text().split()
+    moe_keys = list(cti_b200.SMoE(128, 256, 4).state_dict().keys())
+    enc_keys = list(cti_b200.RepEncoder(100, 8, 0, 28, 16).state_dict().keys())
+    assert moe_keys + enc_keys == ref_keys
+
+
+def test_reference_state_dict_loads_into_drop_in():
+    import golden_inputs as gi
+
+    inp = gi.moe_inputs("moe_config_d128_e8")
+    sd = {"gate.w_g.weight": inp["wg"], "gate.w_g.bias": inp["bg"]}
+    for e in range(8):
+        sd[f"experts.{e}.fc1.weight"] = inp["w1"][e]
+        sd[f"experts.{e}.fc1.bias"] = inp["b1"][e]
+        sd[f"experts.{e}.fc2.weight"] = inp["w2"][e]
+        sd[f"experts.{e}.fc2.bias"] = inp["b2"][e]
+    m = cti_b200.SMoE(128, 256, 8)
+    m.load_state_dict(sd)
+    assert torch.equal(m.experts[3].fc2.weight, inp["w2"][3])
+
+
+def test_forward_refuses_cpu_inputs():
+    m = cti_b200.SMoE(128, 256, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.zeros(1, 4, 128, dtype=torch.bfloat16))
+
+
+def test_only_top2_supported():
+    with pytest.raises(ValueError):
+        cti_b200.SMoE(128, 256, 8, k=3)
+
+
+def test_cfg2_token_set_is_deterministic():
+    T, cu = synth.moe_tokens(synth.CFG2)
+    T2, cu2 = synth.moe_tokens(synth.CFG2)
+    assert T == T2 and torch.equal(cu, cu2)
+    assert cu.dtype == torch.int32 and cu.numel() == 513 and int(cu[-1]) == T
+    assert 512 * 16 <= T <= 512 * 256
+    lens = (cu[1:] - cu[:-1]).numpy()
+    assert lens.min() >= 16 and lens.max() <= 256
+
+
+def test_zipf_router_bias_profile():
+    b = synth.zipf_router_bias(16, 1.2)
+    p = torch.exp(b.double())
+    assert abs(p.sum().item() - 1.0) < 1e-6
+    ps = torch.sort(p, descending=True).values
+    ratio = (ps[0] / ps).numpy()
+    np.testing.assert_allclose(ratio, np.arange(1, 17) ** 1.2, rtol=1e-5)
+
+
+def test_bag_batch_layout_matches_reference_contract():
+    bb = synth.bag_batch(batch=64, seed=1)
+    F, B = bb.features, bb.batch
+    assert bb.row_offsets.numel() == F * (B + 1)
+    offs = bb.row_offsets.view(F, B + 1)
+    assert (offs[:, 0] == 0).all()
+    assert (offs[:, 1:] >= offs[:, :-1]).all()
+    lens = offs[:, -1]
+    assert torch.equal(bb.val_offsets[1:], torch.cumsum(lens, 0)[:-1])
+    assert int(lens.sum()) == bb.values.numel()
+    for f in range(F):
+        v = bb.values[bb.val_offsets[f]:bb.val_offsets[f] + lens[f]]
+        assert v.min() >= 0 and v.max() < bb.vocab[f]
+    assert (bb.vocab >= 1e4 - 1).all() and (bb.vocab <= 2e6 + 1).all()
+
+
+def test_zipf_ids_are_skewed():
+    rng = np.random.default_rng(0)
+    ids = synth.zipf_ids(200000, 10000, 1.1, rng)
+    _, counts = np.unique(ids, return_counts=True)
+    counts = np.sort(counts)[::-1]
+    assert counts[0] > 20 * np.median(counts)
