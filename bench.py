@@ -229,7 +229,9 @@ def workload_config(cfg, T, sample=None):
                      f"experts, d_ff {cfg.dim_ff}, {cfg.samples} packed samples U{{16..256}}",
          "tokens": T, "d_model": cfg.d_model, "experts": cfg.num_experts, "d_ff": cfg.dim_ff,
          "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
-         "l2": "flushed (256 MiB write) before every timed step", "per_gpu": "one replica"}
+         "l2": "flushed (256 MiB write) before every timed step",
+         "host": "enqueue hidden behind a device-side wait before each timed step (value); "
+                 "included in e2e", "per_gpu": "one replica"}
     if sample is not None:
         c["cpu_sample_tokens"] = sample
     return c
@@ -238,12 +240,21 @@ def workload_config(cfg, T, sample=None):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def time_steps(fn, steps, flush, dev):
+def device_wait(dev, ms: float = 1.0) -> None:
+    """Parks the stream for about `ms` (a spin kernel) so the host enqueues
+    the next step while the device waits; the step's events then time device
+    execution only, not host launch latency."""
+    torch.cuda._sleep(int(ms * 2.0e6))
+
+
+def time_steps(fn, steps, flush, dev, hide_host=True):
     """Per-step device time (ms) of fn(), L2 flushed before each step outside
     the event pair."""
     times = []
     for _ in range(steps):
         flush.zero_()
+        if hide_host:
+            device_wait(dev)
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
@@ -255,29 +266,36 @@ def time_steps(fn, steps, flush, dev):
 
 
 def stage_times(m, x2, flush, dev, reps=10):
-    """Mean device time (ms) of each stage launched separately."""
+    """Mean device time (ms) of each stage launched separately, the host
+    enqueue hidden behind a device wait before each stage."""
     from cti_b200 import ops
 
-    names = ["router", "dispatch", "ffn_fc1", "ffn_fc2", "combine"]
-    acc = {n: [] for n in names}
-    for _ in range(reps):
+    fused = m.d_model in (128, 256)
+    acc = {}
+
+    def timed(name, fn):
         flush.zero_()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-        ev[0].record()
-        r = ops.router(x2, m._wg, m._bg, renorm=True)
-        ev[1].record()
-        d = ops.dispatch(x2, r, m.num_experts)
-        ev[2].record()
-        h = ops.grouped_gemm(d.xperm, m._w1, m._b1, d.offsets, act="gelu")
-        ev[3].record()
-        y = ops.grouped_gemm(h, m._w2, m._b2, d.offsets, act="none")
-        ev[4].record()
-        ops.combine(y, d.perm_inv, r.gate2)
-        ev[5].record()
-        torch.cuda.synchronize(dev)
-        for i, n in enumerate(names):
-            acc[n].append(ev[i].elapsed_time(ev[i + 1]))
-    return {n: statistics.mean(v) for n, v in acc.items()}
+        device_wait(dev, 0.5)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = fn()
+        e.record()
+        acc.setdefault(name, []).append((s, e))
+        return out
+
+    for _ in range(reps):
+        r = timed("router", lambda: ops.router(x2, m._wg, m._bg, renorm=True))
+        d = timed("dispatch", lambda: ops.dispatch(x2, r, m.num_experts))
+        if fused:
+            y = timed("ffn_fused", lambda: ops.expert_ffn_fused(
+                d.xperm, m._w1, m._b1, m._w2, m._b2, d.offsets, act="gelu"))
+        h = timed("ffn_fc1", lambda: ops.grouped_gemm(d.xperm, m._w1, m._b1, d.offsets,
+                                                      act="gelu"))
+        y2 = timed("ffn_fc2", lambda: ops.grouped_gemm(h, m._w2, m._b2, d.offsets, act="none"))
+        timed("combine", lambda: ops.combine(y if fused else y2, d.perm_inv, r.gate2))
+    torch.cuda.synchronize(dev)
+    return {n: statistics.mean(s.elapsed_time(e) for s, e in v) for n, v in acc.items()}
 
 
 def run_ours(args, world, rank, local):
@@ -330,7 +348,7 @@ def run_ours(args, world, rank, local):
         e2e_step()
     barrier(world)
     torch.cuda.synchronize(dev)
-    e2e_times = time_steps(e2e_step, args.steps, flush, dev)
+    e2e_times = time_steps(e2e_step, args.steps, flush, dev, hide_host=False)
     barrier(world)
     e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
     e2e_value = tokens_all / (e2e_ms / 1e3)
@@ -338,11 +356,18 @@ def run_ours(args, world, rank, local):
     stages = stage_times(m, x, flush, dev)
     peaks, peak_src = load_peaks()
     R = 2 * T
-    ffn_flops = 2.0 * R * cfg.d_model * cfg.dim_ff  # one of the two expert GEMMs
-    dom = "ffn_fc1" if stages["ffn_fc1"] >= stages["ffn_fc2"] else "ffn_fc2"
-    achieved = ffn_flops / (stages[dom] / 1e3) / 1e12
+    gemm_flops = 2.0 * R * cfg.d_model * cfg.dim_ff  # one of the two expert GEMMs
+    if "ffn_fused" in stages:
+        dom, dom_flops = "ffn_fused", 2 * gemm_flops
+        launches_per_step = 5
+    else:
+        dom = "ffn_fc1" if stages["ffn_fc1"] >= stages["ffn_fc2"] else "ffn_fc2"
+        dom_flops = gemm_flops
+        launches_per_step = 6
+    achieved = dom_flops / (stages[dom] / 1e3) / 1e12
     peak = float(peaks["bf16_tflops"])
-    launches_per_step = 6
+    kernel_names = {"ffn_fused": "fused_ffn_kernel", "ffn_fc1": "grouped_gemm_kernel (fc1)",
+                    "ffn_fc2": "grouped_gemm_kernel (fc2)"}
 
     if rank != 0:
         return
@@ -357,17 +382,51 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": x_h.numel() * x_h.element_size(),
                 "d2h_bytes_per_step": out_h.numel() * out_h.element_size()},
-        "roofline": {"bound": "tensor", "kernel": f"grouped_gemm ({dom})",
+        "roofline": {"bound": "tensor", "kernel": kernel_names[dom],
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": f"bf16_tflops of {peak_src}",
-                     "flops_per_launch": ffn_flops, "traffic": None},
-        "layer_roofline_frac": (2 * ffn_flops / (step_ms / 1e3) / 1e12 / world) / peak,
+                     "flops_per_launch": dom_flops, "traffic": None},
+        "layer_roofline_frac": (2 * gemm_flops * world / (step_ms / 1e3) / 1e12 / world) / peak,
         "stages_ms": stages,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+
+
+def run_profile_workload(args):
+    """--profile STAGE: the configuration-2 workload with one stage launched
+    warmup + steps times and nothing else timed; the small, self-contained
+    command the ncu captures under profiles/ are taken on."""
+    import cti_b200
+    from cti_b200 import _lib, ops, synth
+
+    dev = torch.device("cuda", 0)
+    cfg = synth.CFG2
+    T, _ = synth.moe_tokens(cfg)
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, device=dev)
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts).to(dev)
+    synth.load_moe_module(m, w)
+    m.prepare_for_inference()
+    x = synth.moe_activations(T, cfg.d_model, device=dev)
+    r = ops.router(x, m._wg, m._bg)
+    d = ops.dispatch(x, ops.router(x, m._wg, m._bg), m.num_experts)
+    y = ops.expert_ffn_fused(d.xperm, m._w1, m._b1, m._w2, m._b2, d.offsets)
+    stage = {
+        "router": lambda: ops.router(x, m._wg, m._bg),
+        "dispatch": lambda: ops.dispatch(x, ops.router(x, m._wg, m._bg), m.num_experts),
+        "ffn_fused": lambda: ops.expert_ffn_fused(d.xperm, m._w1, m._b1, m._w2, m._b2,
+                                                  d.offsets, out=y),
+        "ffn_fc1": lambda: ops.grouped_gemm(d.xperm, m._w1, m._b1, d.offsets, act="gelu"),
+        "combine": lambda: ops.combine(y, d.perm_inv, r.gate2),
+        "layer": lambda: m(x.unsqueeze(0)),
+    }[args.profile]
+    for _ in range(args.warmup + args.steps):
+        stage()
+    torch.cuda.synchronize(dev)
+    _lib.raise_on_status(dev)
+    print(f"profile workload {args.profile}: T={T}, {args.warmup + args.steps} launches")
 
 
 def main():
@@ -378,7 +437,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile", default=None,
+                    choices=["router", "dispatch", "ffn_fused", "ffn_fc1", "combine", "layer"],
+                    help="run one stage of the configuration-2 workload for an ncu capture")
     args = ap.parse_args()
+    if args.profile:
+        run_profile_workload(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

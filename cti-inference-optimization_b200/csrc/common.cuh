@@ -217,14 +217,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
 // ---------------------------------------------------------------------------
 // Numerics shared by epilogues.
 // ---------------------------------------------------------------------------
-CTI_DEVICE float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
-
-CTI_DEVICE float apply_act(float x, int act) {
-  if (act == CTI_ACT_GELU) return gelu_erf(x);
-  if (act == CTI_ACT_RELU) return fmaxf(x, 0.0f);
-  return x;
-}
-
 CTI_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

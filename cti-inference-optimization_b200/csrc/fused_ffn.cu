@@ -1,8 +1,449 @@
-// Stage 3 (fused): expert FFN with the hidden tile kept on chip.
+// Stage 3, fused: the whole expert FFN of a 128-row tile in one CTA,
+//
+//   Y[rows] = act(Xp[rows] @ W1[e]^T + b1[e]) @ W2[e]^T + b2[e],
+//
+// with the [128, d_ff] hidden activation never leaving the SM.  The
+// reference writes that hidden tensor to HBM between its fc1 and fc2 Triton
+// GEMMs (packed_hidden, E*T*F elements; online_best/infer.py:2028-2034,
+// :2128-2167); at d_model 256 / d_ff 1024 that round trip alone costs about
+// as much HBM time as the GEMMs' tensor time.
+//
+// Per tile (128 token rows of one expert), d_ff is processed in 128-wide
+// chunks c:
+//   GEMM1(c): acc1[c%2] (TMEM, 128 cols) = X[128, D] @ W1[e][c*128:+128, :]^T
+//   epilogue: acc1 -> +b1 -> GELU -> bf16 -> H[c%2] (shared memory, laid out
+//             exactly as a TMA 128-byte-swizzled K-major tile)
+//   GEMM2(c): acc2 (TMEM, D cols) += H[c%2] @ W2[e][:, c*128:+128]^T
+// The MMA thread issues GEMM1(c+1) before GEMM2(c), so the tensor core works
+// on the next chunk while the epilogue warps run the GELU of this one.
+// After the last chunk, acc2 + b2 is written to Y as bf16.
+//
+// Roles (320 threads): warp 0 TMA producer (X tile once per tile; W1/W2
+// 128x64 slices through a ring of 16 KB stages), warp 1 TMEM owner and MMA
+// issuer (tcgen05.mma M=128 N=128 K=16, bf16 -> fp32), warps 2-9 epilogue
+// (two warps per TMEM lane quadrant, each owning 64 of a chunk's 128 columns
+// and half of the output columns).
+//
+// TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
+// Shared memory (D=256): X 64 KB + H 2x32 KB + ring 5x16 KB + scheduler.
 #include "common.cuh"
+#include "gelu.cuh"
+#include "sched.cuh"
+#include "tmap.cuh"
 
-extern "C" int cti_moe_expert_ffn_fused(const void*, const void*, const float*, const void*,
-                                        const float*, const int32_t*, int, int, int64_t, int, int,
-                                        int, void*, int32_t*, void*) {
-  return CTI_ERR_UNSUPPORTED;
+namespace cti {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kFC = 128;           // d_ff chunk
+constexpr int kBK = 64;            // bf16 elements per 128-byte swizzled row
+constexpr int kSlab = kBM * kBK * 2;  // 16 KB: one 128x64 bf16 tile
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr uint32_t kAcc1Col = 256;
+
+template <int D>
+struct FF {
+  static constexpr int XK = D / kBK;          // X k-slabs
+  static constexpr int HALVES = D / 128;      // GEMM2 N halves of 128
+  static constexpr int STAGES = D == 256 ? 5 : 7;
+  static constexpr size_t X_BYTES = (size_t)XK * kSlab;
+  static constexpr size_t H_BYTES = 2 * (size_t)2 * kSlab;  // two buffers of 128x128
+  static constexpr size_t RING_BYTES = (size_t)STAGES * kSlab;
+  static constexpr size_t SMEM =
+      1024 + X_BYTES + H_BYTES + RING_BYTES + GroupSched::smem_bytes() + 256;
+};
+
+// Writes 64 consecutive bf16 columns (8 chunks of 16 bytes) of row r into a
+// 128x64 K-major slab with the 128-byte swizzle (chunk j of row r lives at
+// chunk position j ^ (r % 8)), the layout TMA produces and UMMA reads.
+CTI_DEVICE void store_row_swizzled(uint8_t* slab, int r, const uint32_t (&w)[32]) {
+  uint8_t* row = slab + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int pos = j ^ (r & 7);
+    *reinterpret_cast<uint4*>(row + pos * 16) =
+        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    fused_ffn_kernel(const __grid_constant__ CUtensorMap tmX,
+                     const __grid_constant__ CUtensorMap tmW1,
+                     const __grid_constant__ CUtensorMap tmW2,
+                     const int32_t* __restrict__ group_offsets, int G, int Gw, int64_t rows_total,
+                     int F, const float* __restrict__ b1, const float* __restrict__ b2, int act,
+                     __nv_bfloat16* __restrict__ Y, int32_t* status) {
+  using P = FF<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sx = smem;
+  uint8_t* sh = sx + P::X_BYTES;
+  uint8_t* ring = sh + P::H_BYTES;
+  uint8_t* sched_mem = ring + P::RING_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + GroupSched::smem_bytes());
+  uint64_t* full = bars;
+  uint64_t* empty = full + P::STAGES;
+  uint64_t* x_full = empty + P::STAGES;
+  uint64_t* x_empty = x_full + 1;
+  uint64_t* a1_full = x_empty + 1;  // [2]
+  uint64_t* a1_empty = a1_full + 2;  // [2]
+  uint64_t* h_full = a1_empty + 2;   // [2]
+  uint64_t* h_empty = h_full + 2;    // [2]
+  uint64_t* a2_full = h_empty + 2;
+  uint64_t* a2_empty = a2_full + 1;
+  uint64_t* drain = a2_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int nch = F / kFC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(x_full, 1);
+    mbar_init(x_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a1_full[i], 1);
+      mbar_init(&a1_empty[i], kEpiThreads);
+      mbar_init(&h_full[i], kEpiThreads);
+      mbar_init(&h_empty[i], 1);
+    }
+    mbar_init(a2_full, 1);
+    mbar_init(a2_empty, kEpiThreads);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x == 32) {
+    prefetch_tensormap(&tmX);
+    prefetch_tensormap(&tmW1);
+    prefetch_tensormap(&tmW2);
+  }
+  GroupSched sched;
+  sched.init(sched_mem, group_offsets, G, rows_total, kBM, 1, status);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = sched.total_tiles();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0, x_issued = 0;
+      int it = 0;
+      bool ok = true;
+      auto load_slab = [&](const CUtensorMap* map, int c0, int c1) -> bool {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, status, 0x201, abort_flag)) return false;
+        mbar_arrive_expect_tx(&full[stage], kSlab);
+        tma_load_2d(ring + stage * kSlab, map, &full[stage], c0, c1);
+        ++issued;
+        if (++stage == P::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        return true;
+      };
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        const TileCoord tc = sched.decode(t);
+        const int gw = tc.g % Gw;
+        if (!mbar_wait(x_empty, (uint32_t)(it & 1) ^ 1u, status, 0x202, abort_flag)) break;
+        mbar_arrive_expect_tx(x_full, (uint32_t)P::X_BYTES);
+        for (int kb = 0; kb < P::XK; ++kb)
+          tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
+        ++x_issued;
+        for (int s = 0; s <= nch && ok; ++s) {
+          if (s < nch) {
+            for (int kb = 0; kb < P::XK && ok; ++kb)
+              ok = load_slab(&tmW1, kb * kBK, gw * F + s * kFC);
+          }
+          if (s >= 1) {
+            const int c = s - 1;
+            for (int kb = 0; kb < 2 && ok; ++kb)
+              for (int hf = 0; hf < P::HALVES && ok; ++hf)
+                ok = load_slab(&tmW2, c * kFC + kb * kBK, gw * D + hf * 128);
+          }
+        }
+      }
+      // Let every load this thread issued land before the CTA can exit.
+      for (int i = 1; i <= P::STAGES && i <= issued; ++i) {
+        const int64_t n = issued - i;
+        mbar_wait(&full[n % P::STAGES], (uint32_t)((n / P::STAGES) & 1), status, 0x203, nullptr);
+      }
+      if (x_issued > 0) mbar_wait(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x204, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, 128);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool any = false, ok = true;
+      const uint32_t x_addr = smem_u32(sx);
+      const uint32_t h_addr = smem_u32(sh);
+      const uint32_t ring_addr = smem_u32(ring);
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        if (!mbar_wait(x_full, (uint32_t)(it & 1), status, 0x205, abort_flag)) break;
+        tc_fence_after();
+        for (int s = 0; s <= nch && ok; ++s) {
+          if (s < nch) {  // GEMM1(s)
+            const int64_t gc = (int64_t)it * nch + s;
+            const int b = (int)(gc & 1);
+            const uint32_t k = (uint32_t)(gc >> 1);
+            if (!mbar_wait(&a1_empty[b], (k & 1u) ^ 1u, status, 0x206, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem_base + kAcc1Col + (uint32_t)b * 128u;
+            for (int kb = 0; kb < P::XK; ++kb) {
+              if (!mbar_wait(&full[stage], phase, status, 0x207, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t a0 = x_addr + kb * kSlab;
+              const uint32_t b0 = ring_addr + stage * kSlab;
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                umma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                          (kb | kk) != 0 ? 1u : 0u);
+              any = true;
+              umma_commit(&empty[stage]);
+              if (++stage == P::STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            umma_commit(&a1_full[b]);
+            if (s == nch - 1) umma_commit(x_empty);
+          }
+          if (s >= 1) {  // GEMM2(s-1)
+            const int c = s - 1;
+            const int64_t gc = (int64_t)it * nch + c;
+            const int b = (int)(gc & 1);
+            const uint32_t k = (uint32_t)(gc >> 1);
+            if (c == 0) {
+              if (!mbar_wait(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x208, abort_flag)) {
+                ok = false;
+                break;
+              }
+            }
+            if (!mbar_wait(&h_full[b], k & 1u, status, 0x209, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            for (int kb = 0; kb < 2 && ok; ++kb) {
+              for (int hf = 0; hf < P::HALVES; ++hf) {
+                if (!mbar_wait(&full[stage], phase, status, 0x20a, abort_flag)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = h_addr + (uint32_t)b * (2 * kSlab) + kb * kSlab;
+                const uint32_t b0 = ring_addr + stage * kSlab;
+                const uint32_t d = tmem_base + (uint32_t)hf * 128u;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                  umma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                            idesc, (c | kb | kk) != 0 ? 1u : 0u);
+                umma_commit(&empty[stage]);
+                if (++stage == P::STAGES) {
+                  stage = 0;
+                  phase ^= 1u;
+                }
+              }
+            }
+            if (!ok) break;
+            umma_commit(&h_empty[b]);
+            if (c == nch - 1) umma_commit(a2_full);
+          }
+        }
+      }
+      if (any) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, status, 0x20b, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;           // 0..7
+    const int q = warp & 3;            // TMEM lane quadrant of this warp
+    const int hs = ew >> 2;            // which half of the columns
+    const int r = q * 32 + lane;       // tile row owned by this thread
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+      const TileCoord tc = sched.decode(t);
+      const int gw = tc.g % Gw;
+      for (int c = 0; c < nch; ++c) {
+        const int64_t gc = (int64_t)it * nch + c;
+        const int b = (int)(gc & 1);
+        const uint32_t k = (uint32_t)(gc >> 1);
+        if (!mbar_wait(&a1_full[b], k & 1u, status, 0x20c, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v0[32], v1[32];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col +
+                               (uint32_t)b * 128u + (uint32_t)hs * 64u;
+        tmem_ld_32x32b_x32(taddr, v0);
+        tmem_ld_32x32b_x32(taddr + 32, v1);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&a1_empty[b]);
+
+        const float4* bias4 =
+            reinterpret_cast<const float4*>(b1 + (int64_t)gw * F + c * kFC + hs * 64);
+        uint32_t w0[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 bb = __ldg(bias4 + j);
+          float a0 = __uint_as_float(v0[4 * j]) + bb.x;
+          float a1 = __uint_as_float(v0[4 * j + 1]) + bb.y;
+          float a2 = __uint_as_float(v0[4 * j + 2]) + bb.z;
+          float a3 = __uint_as_float(v0[4 * j + 3]) + bb.w;
+          act2(act, a0, a1);
+          act2(act, a2, a3);
+          w0[2 * j] = pack_bf16x2(a0, a1);
+          w0[2 * j + 1] = pack_bf16x2(a2, a3);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 bb = __ldg(bias4 + 8 + j);
+          float a0 = __uint_as_float(v1[4 * j]) + bb.x;
+          float a1 = __uint_as_float(v1[4 * j + 1]) + bb.y;
+          float a2 = __uint_as_float(v1[4 * j + 2]) + bb.z;
+          float a3 = __uint_as_float(v1[4 * j + 3]) + bb.w;
+          act2(act, a0, a1);
+          act2(act, a2, a3);
+          w0[16 + 2 * j] = pack_bf16x2(a0, a1);
+          w0[16 + 2 * j + 1] = pack_bf16x2(a2, a3);
+        }
+        if (!mbar_wait(&h_empty[b], (k & 1u) ^ 1u, status, 0x20d, abort_flag)) {
+          ok = false;
+          break;
+        }
+        store_row_swizzled(sh + (size_t)b * (2 * kSlab) + (size_t)hs * kSlab, r, w0);
+        fence_proxy_async_smem();
+        mbar_arrive(&h_full[b]);
+      }
+      if (!ok) break;
+
+      // Output: acc2 + b2 -> bf16 rows of Y.
+      if (!mbar_wait(a2_full, (uint32_t)(it & 1), status, 0x20e, abort_flag)) break;
+      tc_fence_after();
+      constexpr int kCols = D / 2;  // columns of Y owned by this thread
+      uint32_t o[kCols];
+      const uint32_t taddr2 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)hs * kCols;
+#pragma unroll
+      for (int j = 0; j < kCols / 32; ++j) {
+        uint32_t tmp[32];
+        tmem_ld_32x32b_x32(taddr2 + 32 * j, tmp);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[32 * j + i] = tmp[i];
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(a2_empty);
+      if (r < tc.rows) {
+        const float4* bias4 = reinterpret_cast<const float4*>(b2 + (int64_t)gw * D + hs * kCols);
+        uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)tc.row0 + r) * D + hs * kCols);
+#pragma unroll
+        for (int j = 0; j < kCols / 8; ++j) {
+          const float4 ba = __ldg(bias4 + 2 * j);
+          const float4 bb = __ldg(bias4 + 2 * j + 1);
+          uint4 pk;
+          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + ba.x, __uint_as_float(o[8 * j + 1]) + ba.y);
+          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + ba.z,
+                             __uint_as_float(o[8 * j + 3]) + ba.w);
+          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + bb.x,
+                             __uint_as_float(o[8 * j + 5]) + bb.y);
+          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + bb.z,
+                             __uint_as_float(o[8 * j + 7]) + bb.w);
+          dst[j] = pk;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+template <int D>
+int launch_fused(const void* Xp, const void* W1, const float* b1, const void* W2, const float* b2,
+                 const int32_t* offs, int G, int Gw, int64_t rows_total, int F, int act, void* Y,
+                 int32_t* status, cudaStream_t s) {
+  using P = FF<D>;
+  CUtensorMap tmX, tmW1, tmW2;
+  if (!make_tmap_bf16_2d(&tmX, Xp, (uint64_t)rows_total, D, D, kBM, kBK) ||
+      !make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, D, D, 128, kBK) ||
+      !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * D, (uint64_t)F, (uint64_t)F, 128, kBK))
+    return CTI_ERR_INVALID_ARG;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(fused_ffn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)P::SMEM) != cudaSuccess)
+      return CTI_ERR_CUDA;
+    attr_set = true;
+  }
+  const int sms = device_sm_count();
+  if (sms <= 0) return CTI_ERR_CUDA;
+  const int64_t max_tiles = (rows_total + kBM - 1) / kBM + G;
+  const int grid = (int)(max_tiles < sms ? max_tiles : sms);
+  fused_ffn_kernel<D><<<grid, kThreads, P::SMEM, s>>>(tmX, tmW1, tmW2, offs, G, Gw, rows_total, F,
+                                                       b1, b2, act,
+                                                       static_cast<__nv_bfloat16*>(Y), status);
+  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace cti
+
+extern "C" int cti_moe_expert_ffn_fused(const void* Xp_bf16, const void* W1_bf16, const float* b1,
+                                        const void* W2_bf16, const float* b2,
+                                        const int32_t* group_offsets, int G, int Gw,
+                                        int64_t rows_total, int D, int F, int act, void* Y_bf16,
+                                        int32_t* status, void* stream) {
+  using namespace cti;
+  if (G < 1 || G > GroupSched::kMaxGroups || Gw < 1 || rows_total < 0 || F <= 0)
+    return CTI_ERR_INVALID_ARG;
+  if (act < CTI_ACT_NONE || act > CTI_ACT_GELU) return CTI_ERR_INVALID_ARG;
+  if ((D != 128 && D != 256) || F % kFC != 0) return CTI_ERR_UNSUPPORTED;
+  if (rows_total >= ((int64_t)1 << 31) - 256) return CTI_ERR_UNSUPPORTED;
+  if (!W1_bf16 || !W2_bf16 || !b1 || !b2 || !group_offsets || !Y_bf16) return CTI_ERR_INVALID_ARG;
+  if (rows_total == 0) return CTI_OK;
+  if (!Xp_bf16) return CTI_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(Y_bf16) & 15) || (reinterpret_cast<uintptr_t>(b1) & 15) ||
+      (reinterpret_cast<uintptr_t>(b2) & 15))
+    return CTI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 256)
+    return launch_fused<256>(Xp_bf16, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw, rows_total,
+                             F, act, Y_bf16, status, s);
+  return launch_fused<128>(Xp_bf16, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw, rows_total, F,
+                           act, Y_bf16, status, s);
 }

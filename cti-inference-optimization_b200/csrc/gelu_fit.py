@@ -1,0 +1,61 @@
+"""Derives the polynomial of the GELU epilogue (csrc/gelu.cuh).
+
+GELU(x) = x * Phi(x), Phi(x) = 1 - erfc(x/sqrt2)/2 for x >= 0 and
+erfc(|x|/sqrt2)/2 for x < 0.  With u = |x|,
+
+    erfc(u/sqrt2) = erfcx(u/sqrt2) * exp(-u^2/2)
+                  = 2^( Q(u) - u^2 * log2(e)/2 ),   Q(u) = log2(erfcx(u/sqrt2)),
+
+where erfcx(z) = exp(z^2) erfc(z) is smooth and slowly varying.  Q is
+approximated on [0, U0] by a Chebyshev least-squares fit of degree DEG,
+converted to monomial coefficients for Horner evaluation in fp32.  Beyond
+U0, erfc(u/sqrt2) < 1.3e-15 and u is clamped inside Q only.
+
+Run:  python csrc/gelu_fit.py   (prints the coefficient table and the
+fp32-simulated error of GELU against the exact function).
+"""
+import numpy as np
+from numpy.polynomial import chebyshev as C
+from numpy.polynomial import polynomial as P
+from scipy.special import erfc, erfcx
+
+U0 = 8.0
+DEG = 10
+
+
+def fit():
+    u = np.linspace(0.0, U0, 400001)
+    q = np.log2(erfcx(u / np.sqrt(2.0)))
+    c = C.chebfit(u * (2.0 / U0) - 1.0, q, DEG)
+    mono_t = C.cheb2poly(c)
+    pu = np.zeros(1)
+    for k, ck in enumerate(mono_t):
+        pu = P.polyadd(pu, ck * P.polypow([-1.0, 2.0 / U0], k))
+    return pu.astype(np.float32)
+
+
+def gelu_fp32(x, coef):
+    x = x.astype(np.float32)
+    u = np.abs(x)
+    uc = np.minimum(u, np.float32(U0))
+    acc = np.full_like(x, coef[-1])
+    for ck in coef[-2::-1]:
+        acc = (acc * uc + ck).astype(np.float32)
+    e = np.exp2((acc - u * u * np.float32(0.5 * np.log2(np.e))).astype(np.float32)).astype(np.float32)
+    h = np.float32(0.5) * e
+    phi = np.where(x >= 0, np.float32(1.0) - h, h).astype(np.float32)
+    return (x * phi).astype(np.float32)
+
+
+if __name__ == "__main__":
+    coef = fit()
+    x = np.linspace(-12, 12, 2_000_001)
+    exact = x * 0.5 * erfc(-x / np.sqrt(2.0))  # no cancellation for x << 0
+    g = gelu_fp32(x, coef).astype(np.float64)
+    abs_err = np.abs(g - exact)
+    rel = abs_err / np.maximum(np.abs(exact), 1e-30)
+    print("coefficients (u^0 .. u^%d):" % DEG)
+    for k, ck in enumerate(coef):
+        print(f"  {float(ck)!r}f,  // u^{k}")
+    print(f"max abs err {abs_err.max():.3e}; max rel err on [-U0, U0] "
+          f"{rel[np.abs(x) <= U0].max():.3e}")

@@ -23,6 +23,7 @@
 // of its group; TMA zero-fills rows past the end of A, and the epilogue
 // stores only the group's own rows.
 #include "common.cuh"
+#include "gelu.cuh"
 #include "sched.cuh"
 #include "tmap.cuh"
 
@@ -209,8 +210,9 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float lo = apply_act(__uint_as_float(v[2 * j]) + bv[2 * j], act);
-            const float hi = apply_act(__uint_as_float(v[2 * j + 1]) + bv[2 * j + 1], act);
+            float lo = __uint_as_float(v[2 * j]) + bv[2 * j];
+            float hi = __uint_as_float(v[2 * j + 1]) + bv[2 * j + 1];
+            act2(act, lo, hi);
             packed[j] = pack_bf16x2(lo, hi);
           }
           uint4* dst = reinterpret_cast<uint4*>(crow + c * 32);

@@ -1,0 +1,104 @@
+"""Stage 3 fused expert FFN (fc1 -> GELU -> fc2 with the hidden tile kept in
+shared memory) on the B200 vs a torch fp32 reference of the same op.
+Tolerance: max rel err 1e-2 (bf16 hidden activations and bf16 output vs
+fp32 throughout)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from helpers import max_rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def ref_ffn(x, w1, b1, w2, b2, offs, act, Gw):
+    out = torch.zeros(x.shape[0], w2.shape[1])
+    o = offs.tolist()
+    for g in range(len(o) - 1):
+        lo, hi = o[g], o[g + 1]
+        if hi <= lo:
+            continue
+        e = g % Gw
+        h = x[lo:hi].float() @ w1[e].float().T + b1[e]
+        h = F.gelu(h) if act == "gelu" else F.relu(h) if act == "relu" else h
+        out[lo:hi] = h @ w2[e].float().T + b2[e]
+    return out
+
+
+CASES = [
+    # D, F, group sizes, Gw, act
+    (256, 128, [128], 1, "gelu"),
+    (256, 1024, [128], 1, "gelu"),
+    (128, 512, [1, 0, 200, 55], 4, "gelu"),
+    (256, 1024, [300, 0, 1000, 17, 128, 129, 5000, 2, 900, 0, 0, 33, 64, 65, 700, 1], 16, "gelu"),
+    (256, 512, [640, 640, 384], 3, "relu"),
+    (128, 256, [3000, 2000, 1000], 3, "none"),
+    (256, 1024, [40000, 30000, 20000, 10000], 4, "gelu"),
+]
+
+
+@pytest.mark.parametrize("D,Fd,sizes,Gw,act", CASES)
+def test_fused_ffn_matches_fp32(cuda_device, D, Fd, sizes, Gw, act):
+    from cti_b200 import _lib, ops
+
+    rows = sum(sizes)
+    g = torch.Generator().manual_seed(rows + D + Fd)
+    x = torch.randn(rows, D, generator=g).bfloat16()
+    w1 = (torch.randn(Gw, Fd, D, generator=g) * 0.05).bfloat16()
+    b1 = torch.randn(Gw, Fd, generator=g) * 0.1
+    w2 = (torch.randn(Gw, D, Fd, generator=g) * 0.05).bfloat16()
+    b2 = torch.randn(Gw, D, generator=g) * 0.1
+    offs = torch.zeros(len(sizes) + 1, dtype=torch.int32)
+    offs[1:] = torch.cumsum(torch.tensor(sizes), 0)
+    dev = cuda_device
+    y = ops.expert_ffn_fused(x.to(dev), w1.to(dev), b1.to(dev), w2.to(dev), b2.to(dev),
+                             offs.to(dev), act=act)
+    _lib.raise_on_status(dev)
+    ref = ref_ffn(x, w1, b1, w2, b2, offs, act, Gw)
+    err = max_rel_err(y, ref)
+    assert err < TOL, f"max rel err {err}"
+
+
+def test_fused_ffn_agrees_with_two_gemms(cuda_device):
+    """The fused path and the two-GEMM path round the hidden activation to
+    bf16 at the same point, so they agree to accumulation-order noise."""
+    from cti_b200 import _lib, ops
+
+    dev = cuda_device
+    rows, D, Fd, E = 6000, 256, 1024, 16
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(rows, D, generator=g, device=dev).bfloat16()
+    w1 = (torch.randn(E, Fd, D, generator=g, device=dev) * 0.05).bfloat16()
+    b1 = torch.randn(E, Fd, generator=g, device=dev) * 0.1
+    w2 = (torch.randn(E, D, Fd, generator=g, device=dev) * 0.05).bfloat16()
+    b2 = torch.randn(E, D, generator=g, device=dev) * 0.1
+    offs = torch.linspace(0, rows, E + 1, device=dev).round().int()
+    y1 = ops.expert_ffn_fused(x, w1, b1, w2, b2, offs, act="gelu")
+    h = ops.grouped_gemm(x, w1, b1, offs, act="gelu")
+    y2 = ops.grouped_gemm(h, w2, b2, offs, act="none")
+    _lib.raise_on_status(dev)
+    assert max_rel_err(y1, y2) < 4e-3
+
+
+def test_gelu_epilogue_accuracy(cuda_device):
+    """GELU of the epilogue vs the exact erf GELU (fp64): a GEMM with an
+    identity weight block returns gelu(x + b) rounded to bf16, which must be
+    the correctly rounded value up to one bf16 ulp."""
+    from cti_b200 import _lib, ops
+
+    dev = cuda_device
+    xs = torch.linspace(-8.0, 8.0, 128 * 64 * 8).reshape(-1, 64)
+    a = xs.bfloat16()
+    w = torch.zeros(1, 128, 64)
+    w[0, :64, :64] = torch.eye(64)
+    w[0, 64:, :64] = torch.eye(64)
+    offs = torch.tensor([0, a.shape[0]], dtype=torch.int32)
+    out = ops.grouped_gemm(a.to(dev), w.bfloat16().to(dev), None, offs.to(dev), act="gelu")
+    _lib.raise_on_status(dev)
+    xa = a.double()
+    exact = xa * 0.5 * torch.special.erfc(-xa / 2 ** 0.5)
+    got = out[:, :64].double().cpu()
+    ulp = exact.abs().clamp_min(1e-30) * 2.0 ** -7
+    assert ((got - exact).abs() <= ulp + 1e-30).all()
+    assert torch.equal(out[:, :64].cpu(), out[:, 64:].cpu())
