@@ -266,36 +266,41 @@ def time_steps(fn, steps, flush, dev, hide_host=True):
 
 
 def stage_times(m, x2, flush, dev, reps=10):
-    """Mean device time (ms) of each stage launched separately, the host
-    enqueue hidden behind a device wait before each stage."""
+    """Median device time (ms) of each stage launched on its own: every stage
+    runs once untimed first (module loading), and each timed launch sits
+    behind an L2 flush and a device wait that hides the host enqueue."""
     from cti_b200 import ops
 
     fused = m.d_model in (128, 256)
     acc = {}
 
-    def timed(name, fn):
+    def timed(name, fn, record=True):
         flush.zero_()
-        device_wait(dev, 0.5)
+        device_wait(dev, 1.0)
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
         out = fn()
         e.record()
-        acc.setdefault(name, []).append((s, e))
+        if record:
+            acc.setdefault(name, []).append((s, e))
         return out
 
-    for _ in range(reps):
-        r = timed("router", lambda: ops.router(x2, m._wg, m._bg, renorm=True))
-        d = timed("dispatch", lambda: ops.dispatch(x2, r, m.num_experts))
+    for rep in range(reps + 1):
+        rec = rep > 0
+        r = timed("router", lambda: ops.router(x2, m._wg, m._bg, renorm=True), rec)
+        d = timed("dispatch", lambda: ops.dispatch(x2, r, m.num_experts), rec)
+        y = None
         if fused:
             y = timed("ffn_fused", lambda: ops.expert_ffn_fused(
-                d.xperm, m._w1, m._b1, m._w2, m._b2, d.offsets, act="gelu"))
+                d.xperm, m._w1, m._b1, m._w2, m._b2, d.offsets, act="gelu"), rec)
         h = timed("ffn_fc1", lambda: ops.grouped_gemm(d.xperm, m._w1, m._b1, d.offsets,
-                                                      act="gelu"))
-        y2 = timed("ffn_fc2", lambda: ops.grouped_gemm(h, m._w2, m._b2, d.offsets, act="none"))
-        timed("combine", lambda: ops.combine(y if fused else y2, d.perm_inv, r.gate2))
+                                                      act="gelu"), rec)
+        y2 = timed("ffn_fc2", lambda: ops.grouped_gemm(h, m._w2, m._b2, d.offsets, act="none"),
+                   rec)
+        timed("combine", lambda: ops.combine(y if fused else y2, d.perm_inv, r.gate2), rec)
     torch.cuda.synchronize(dev)
-    return {n: statistics.mean(s.elapsed_time(e) for s, e in v) for n, v in acc.items()}
+    return {n: statistics.median(s.elapsed_time(e) for s, e in v) for n, v in acc.items()}
 
 
 def run_ours(args, world, rank, local):

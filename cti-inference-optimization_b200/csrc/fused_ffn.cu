@@ -18,14 +18,16 @@
 // on the next chunk while the epilogue warps run the GELU of this one.
 // After the last chunk, acc2 + b2 is written to Y as bf16.
 //
-// Roles (320 threads): warp 0 TMA producer (X tile once per tile; W1/W2
+// Roles (576 threads): warp 0 TMA producer (X tile once per tile; W1/W2
 // 128x64 slices through a ring of 16 KB stages), warp 1 TMEM owner and MMA
-// issuer (tcgen05.mma M=128 N=128 K=16, bf16 -> fp32), warps 2-9 epilogue
-// (two warps per TMEM lane quadrant, each owning 64 of a chunk's 128 columns
-// and half of the output columns).
+// issuer (tcgen05.mma M=128 N=128 K=16, bf16 -> fp32), warps 2-17 epilogue
+// (four warps per TMEM lane quadrant, each owning 32 of a chunk's 128
+// columns and a quarter of the output columns; the expert's biases are
+// staged in shared memory once per expert change).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
-// Shared memory (D=256): X 64 KB + H 2x32 KB + ring 5x16 KB + scheduler.
+// Shared memory (D=256): X 64 KB + H 2x32 KB + ring 5x16 KB + biases 5 KB +
+// scheduler 2 KB.  d_ff <= 1024 (one expert's b1 in shared memory).
 #include "common.cuh"
 #include "gelu.cuh"
 #include "sched.cuh"
@@ -38,7 +40,9 @@ constexpr int kBM = 128;
 constexpr int kFC = 128;           // d_ff chunk
 constexpr int kBK = 64;            // bf16 elements per 128-byte swizzled row
 constexpr int kSlab = kBM * kBK * 2;  // 16 KB: one 128x64 bf16 tile
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kMaxF = 1024;  // b1 of one expert staged in shared memory
+using Sched = GroupSchedT<256>;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr uint32_t kAcc1Col = 256;
@@ -51,18 +55,20 @@ struct FF {
   static constexpr size_t X_BYTES = (size_t)XK * kSlab;
   static constexpr size_t H_BYTES = 2 * (size_t)2 * kSlab;  // two buffers of 128x128
   static constexpr size_t RING_BYTES = (size_t)STAGES * kSlab;
+  static constexpr size_t BIAS_BYTES = (size_t)(kMaxF + D) * 4;
   static constexpr size_t SMEM =
-      1024 + X_BYTES + H_BYTES + RING_BYTES + GroupSched::smem_bytes() + 256;
+      1024 + X_BYTES + H_BYTES + RING_BYTES + BIAS_BYTES + Sched::smem_bytes() + 256;
 };
 
-// Writes 64 consecutive bf16 columns (8 chunks of 16 bytes) of row r into a
-// 128x64 K-major slab with the 128-byte swizzle (chunk j of row r lives at
-// chunk position j ^ (r % 8)), the layout TMA produces and UMMA reads.
-CTI_DEVICE void store_row_swizzled(uint8_t* slab, int r, const uint32_t (&w)[32]) {
+// Writes 32 consecutive bf16 columns (four 16-byte chunks, starting at
+// chunk j0 of the row) of row r into a 128x64 K-major slab with the
+// 128-byte swizzle (chunk j of row r lives at chunk position j ^ (r % 8)),
+// the layout TMA produces and UMMA reads.
+CTI_DEVICE void store_row32_swizzled(uint8_t* slab, int r, int j0, const uint32_t (&w)[16]) {
   uint8_t* row = slab + r * 128;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int pos = j ^ (r & 7);
+  for (int j = 0; j < 4; ++j) {
+    const int pos = (j0 + j) ^ (r & 7);
     *reinterpret_cast<uint4*>(row + pos * 16) =
         make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
   }
@@ -83,8 +89,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sx = smem;
   uint8_t* sh = sx + P::X_BYTES;
   uint8_t* ring = sh + P::H_BYTES;
-  uint8_t* sched_mem = ring + P::RING_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + GroupSched::smem_bytes());
+  float* b1s = reinterpret_cast<float*>(ring + P::RING_BYTES);
+  float* b2s = b1s + kMaxF;
+  uint8_t* sched_mem = reinterpret_cast<uint8_t*>(b2s + D);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + Sched::smem_bytes());
   uint64_t* full = bars;
   uint64_t* empty = full + P::STAGES;
   uint64_t* x_full = empty + P::STAGES;
@@ -96,7 +104,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* a2_full = h_empty + 2;
   uint64_t* a2_empty = a2_full + 1;
   uint64_t* drain = a2_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* bfree = drain + 1;   // epilogue threads done with the staged biases
+  uint64_t* bready = bfree + 1;  // new biases staged
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -119,6 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(a2_full, 1);
     mbar_init(a2_empty, kEpiThreads);
     mbar_init(drain, 1);
+    mbar_init(bfree, kEpiThreads);
+    mbar_init(bready, kEpiThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -127,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmW1);
     prefetch_tensormap(&tmW2);
   }
-  GroupSched sched;
+  Sched sched;
   sched.init(sched_mem, group_offsets, G, rows_total, kBM, 1, status);
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -284,15 +296,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;           // 0..7
+    // 16 warps: four per TMEM lane quadrant q; warp group `sub` owns chunk
+    // columns [sub*32, sub*32+32) and output columns [sub*D/4, (sub+1)*D/4).
+    const int ew = warp - 2;           // 0..15
     const int q = warp & 3;            // TMEM lane quadrant of this warp
-    const int hs = ew >> 2;            // which half of the columns
+    const int sub = ew >> 2;           // 0..3
     const int r = q * 32 + lane;       // tile row owned by this thread
+    const int etid = ew * 32 + lane;   // 0..511
+    constexpr int kOutCols = D / 4;
     int it = 0;
+    int staged_gw = -1;
+    uint32_t n_staged = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
       const TileCoord tc = sched.decode(t);
       const int gw = tc.g % Gw;
+      if (gw != staged_gw) {  // the same decision in every epilogue thread
+        if (n_staged > 0) {   // everyone is done with the previous expert's biases
+          mbar_arrive(bfree);
+          if (!mbar_wait(bfree, (n_staged - 1) & 1u, status, 0x20f, abort_flag)) break;
+        }
+        for (int i = etid; i < F; i += kEpiThreads) b1s[i] = b1[(int64_t)gw * F + i];
+        for (int i = etid; i < D; i += kEpiThreads) b2s[i] = b2[(int64_t)gw * D + i];
+        mbar_arrive(bready);
+        if (!mbar_wait(bready, n_staged & 1u, status, 0x210, abort_flag)) break;
+        ++n_staged;
+        staged_gw = gw;
+      }
       for (int c = 0; c < nch; ++c) {
         const int64_t gc = (int64_t)it * nch + c;
         const int b = (int)(gc & 1);
@@ -302,47 +332,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        uint32_t v0[32], v1[32];
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col +
-                               (uint32_t)b * 128u + (uint32_t)hs * 64u;
-        tmem_ld_32x32b_x32(taddr, v0);
-        tmem_ld_32x32b_x32(taddr + 32, v1);
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col + (uint32_t)b * 128u +
+                               (uint32_t)sub * 32u,
+                           v);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&a1_empty[b]);
 
-        const float4* bias4 =
-            reinterpret_cast<const float4*>(b1 + (int64_t)gw * F + c * kFC + hs * 64);
-        uint32_t w0[32];
+        const float* bc = b1s + c * kFC + sub * 32;
+        uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 bb = __ldg(bias4 + j);
-          float a0 = __uint_as_float(v0[4 * j]) + bb.x;
-          float a1 = __uint_as_float(v0[4 * j + 1]) + bb.y;
-          float a2 = __uint_as_float(v0[4 * j + 2]) + bb.z;
-          float a3 = __uint_as_float(v0[4 * j + 3]) + bb.w;
-          act2(act, a0, a1);
-          act2(act, a2, a3);
-          w0[2 * j] = pack_bf16x2(a0, a1);
-          w0[2 * j + 1] = pack_bf16x2(a2, a3);
-        }
+        for (int h = 0; h < 2; ++h) {
+          float a[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 bb = __ldg(bias4 + 8 + j);
-          float a0 = __uint_as_float(v1[4 * j]) + bb.x;
-          float a1 = __uint_as_float(v1[4 * j + 1]) + bb.y;
-          float a2 = __uint_as_float(v1[4 * j + 2]) + bb.z;
-          float a3 = __uint_as_float(v1[4 * j + 3]) + bb.w;
-          act2(act, a0, a1);
-          act2(act, a2, a3);
-          w0[16 + 2 * j] = pack_bf16x2(a0, a1);
-          w0[16 + 2 * j + 1] = pack_bf16x2(a2, a3);
+          for (int i = 0; i < 16; ++i) a[i] = __uint_as_float(v[16 * h + i]) + bc[16 * h + i];
+          act_n<16>(act, a);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[8 * h + i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
         }
         if (!mbar_wait(&h_empty[b], (k & 1u) ^ 1u, status, 0x20d, abort_flag)) {
           ok = false;
           break;
         }
-        store_row_swizzled(sh + (size_t)b * (2 * kSlab) + (size_t)hs * kSlab, r, w0);
+        store_row32_swizzled(sh + (size_t)b * (2 * kSlab) + (size_t)(sub >> 1) * kSlab, r,
+                             (sub & 1) * 4, w);
         fence_proxy_async_smem();
         mbar_arrive(&h_full[b]);
       }
@@ -351,11 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Output: acc2 + b2 -> bf16 rows of Y.
       if (!mbar_wait(a2_full, (uint32_t)(it & 1), status, 0x20e, abort_flag)) break;
       tc_fence_after();
-      constexpr int kCols = D / 2;  // columns of Y owned by this thread
-      uint32_t o[kCols];
-      const uint32_t taddr2 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)hs * kCols;
+      uint32_t o[kOutCols];
+      const uint32_t taddr2 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)sub * kOutCols;
 #pragma unroll
-      for (int j = 0; j < kCols / 32; ++j) {
+      for (int j = 0; j < kOutCols / 32; ++j) {
         uint32_t tmp[32];
         tmem_ld_32x32b_x32(taddr2 + 32 * j, tmp);
 #pragma unroll
@@ -365,20 +378,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(a2_empty);
       if (r < tc.rows) {
-        const float4* bias4 = reinterpret_cast<const float4*>(b2 + (int64_t)gw * D + hs * kCols);
-        uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)tc.row0 + r) * D + hs * kCols);
+        const float* bo = b2s + sub * kOutCols;
+        uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)tc.row0 + r) * D + sub * kOutCols);
 #pragma unroll
-        for (int j = 0; j < kCols / 8; ++j) {
-          const float4 ba = __ldg(bias4 + 2 * j);
-          const float4 bb = __ldg(bias4 + 2 * j + 1);
+        for (int j = 0; j < kOutCols / 8; ++j) {
           uint4 pk;
-          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + ba.x, __uint_as_float(o[8 * j + 1]) + ba.y);
-          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + ba.z,
-                             __uint_as_float(o[8 * j + 3]) + ba.w);
-          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + bb.x,
-                             __uint_as_float(o[8 * j + 5]) + bb.y);
-          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + bb.z,
-                             __uint_as_float(o[8 * j + 7]) + bb.w);
+          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + bo[8 * j],
+                             __uint_as_float(o[8 * j + 1]) + bo[8 * j + 1]);
+          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + bo[8 * j + 2],
+                             __uint_as_float(o[8 * j + 3]) + bo[8 * j + 3]);
+          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + bo[8 * j + 4],
+                             __uint_as_float(o[8 * j + 5]) + bo[8 * j + 5]);
+          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + bo[8 * j + 6],
+                             __uint_as_float(o[8 * j + 7]) + bo[8 * j + 7]);
           dst[j] = pk;
         }
       }
@@ -429,10 +441,10 @@ extern "C" int cti_moe_expert_ffn_fused(const void* Xp_bf16, const void* W1_bf16
                                         int64_t rows_total, int D, int F, int act, void* Y_bf16,
                                         int32_t* status, void* stream) {
   using namespace cti;
-  if (G < 1 || G > GroupSched::kMaxGroups || Gw < 1 || rows_total < 0 || F <= 0)
-    return CTI_ERR_INVALID_ARG;
+  if (G < 1 || Gw < 1 || rows_total < 0 || F <= 0) return CTI_ERR_INVALID_ARG;
   if (act < CTI_ACT_NONE || act > CTI_ACT_GELU) return CTI_ERR_INVALID_ARG;
-  if ((D != 128 && D != 256) || F % kFC != 0) return CTI_ERR_UNSUPPORTED;
+  if ((D != 128 && D != 256) || F % kFC != 0 || F > kMaxF || G > Sched::kMaxGroups)
+    return CTI_ERR_UNSUPPORTED;
   if (rows_total >= ((int64_t)1 << 31) - 256) return CTI_ERR_UNSUPPORTED;
   if (!W1_bf16 || !W2_bf16 || !b1 || !b2 || !group_offsets || !Y_bf16) return CTI_ERR_INVALID_ARG;
   if (rows_total == 0) return CTI_OK;

@@ -47,47 +47,74 @@ CTI_DEVICE uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
+CTI_DEVICE uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+CTI_DEVICE uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 CTI_DEVICE float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-CTI_DEVICE float gelu_finish(float x, float q) {
-  const float h = 0.5f * ex2_approx(q);
-  const float phi = x >= 0.0f ? 1.0f - h : h;
-  return x * phi;
+CTI_DEVICE float copysign_bits(float mag, float sgn) {
+  return __uint_as_float((__float_as_uint(mag) & 0x7fffffffu) |
+                         (__float_as_uint(sgn) & 0x80000000u));
+}
+
+// In-place GELU of N values (N even), ordered so that the N/2 packed Horner
+// chains interleave: every step issues N/2 independent f32x2 FMAs.
+//   Phi(x) = 0.5 + sign(x) * (0.5 - erfc(|x|/sqrt2)/2)
+template <int N>
+CTI_DEVICE void gelu_n(float (&v)[N]) {
+  using namespace gelu_detail;
+  constexpr int P = N / 2;
+  uint64_t uc[P], acc[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    uc[p] = f2_pack(fminf(fabsf(v[2 * p]), kU0), fminf(fabsf(v[2 * p + 1]), kU0));
+    acc[p] = f2_pack(C10, C10);
+  }
+  const float coef[10] = {C9, C8, C7, C6, C5, C4, C3, C2, C1, C0};
+#pragma unroll
+  for (int k = 0; k < 10; ++k) {
+    const uint64_t ck = f2_pack(coef[k], coef[k]);
+#pragma unroll
+    for (int p = 0; p < P; ++p) acc[p] = f2_fma(acc[p], uc[p], ck);
+  }
+  const uint64_t neg_half_log2e = f2_pack(kNegHalfLog2e, kNegHalfLog2e);
+  const uint64_t m_half = f2_pack(-0.5f, -0.5f);
+  const uint64_t half = f2_pack(0.5f, 0.5f);
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    const uint64_t x = f2_pack(v[2 * p], v[2 * p + 1]);
+    const uint64_t q = f2_fma(f2_mul(x, x), neg_half_log2e, acc[p]);
+    float q0, q1;
+    f2_unpack(q, q0, q1);
+    // t = 0.5 - erfc/2 (>= 0); Phi = 0.5 + copysign(t, x).
+    const uint64_t t = f2_fma(f2_pack(ex2_approx(q0), ex2_approx(q1)), m_half, half);
+    float t0, t1;
+    f2_unpack(t, t0, t1);
+    const uint64_t phi =
+        f2_add(f2_pack(copysign_bits(t0, v[2 * p]), copysign_bits(t1, v[2 * p + 1])), half);
+    f2_unpack(f2_mul(x, phi), v[2 * p], v[2 * p + 1]);
+  }
 }
 
 // GELU of two values.
 CTI_DEVICE void gelu2(float x0, float x1, float& g0, float& g1) {
-  using namespace gelu_detail;
-  const float u0 = fabsf(x0), u1 = fabsf(x1);
-  const uint64_t uc = f2_pack(fminf(u0, kU0), fminf(u1, kU0));
-  uint64_t acc = f2_pack(C10, C10);
-  acc = f2_fma(acc, uc, f2_pack(C9, C9));
-  acc = f2_fma(acc, uc, f2_pack(C8, C8));
-  acc = f2_fma(acc, uc, f2_pack(C7, C7));
-  acc = f2_fma(acc, uc, f2_pack(C6, C6));
-  acc = f2_fma(acc, uc, f2_pack(C5, C5));
-  acc = f2_fma(acc, uc, f2_pack(C4, C4));
-  acc = f2_fma(acc, uc, f2_pack(C3, C3));
-  acc = f2_fma(acc, uc, f2_pack(C2, C2));
-  acc = f2_fma(acc, uc, f2_pack(C1, C1));
-  acc = f2_fma(acc, uc, f2_pack(C0, C0));
-  const uint64_t u = f2_pack(u0, u1);
-  const uint64_t uu = f2_fma(u, u, f2_pack(0.0f, 0.0f));
-  const uint64_t q = f2_fma(uu, f2_pack(kNegHalfLog2e, kNegHalfLog2e), acc);
-  float q0, q1;
-  f2_unpack(q, q0, q1);
-  g0 = gelu_finish(x0, q0);
-  g1 = gelu_finish(x1, q1);
-}
-
-CTI_DEVICE float gelu1(float x) {
-  float g0, g1;
-  gelu2(x, 0.0f, g0, g1);
-  return g0;
+  float v[2] = {x0, x1};
+  gelu_n<2>(v);
+  g0 = v[0];
+  g1 = v[1];
 }
 
 // Epilogue activation of a pair (CTI_ACT_*).
@@ -97,6 +124,17 @@ CTI_DEVICE void act2(int act, float& a, float& b) {
   } else if (act == CTI_ACT_RELU) {
     a = fmaxf(a, 0.0f);
     b = fmaxf(b, 0.0f);
+  }
+}
+
+// Epilogue activation of N values.
+template <int N>
+CTI_DEVICE void act_n(int act, float (&v)[N]) {
+  if (act == CTI_ACT_GELU) {
+    gelu_n<N>(v);
+  } else if (act == CTI_ACT_RELU) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = fmaxf(v[i], 0.0f);
   }
 }
 

@@ -20,8 +20,9 @@ struct TileCoord {
   int n_idx;  // n-tile index
 };
 
-struct GroupSched {
-  static constexpr int kMaxGroups = 1024;
+template <int MAXG>
+struct GroupSchedT {
+  static constexpr int kMaxGroups = MAXG;
   __host__ __device__ static constexpr size_t smem_bytes() { return (size_t)2 * (kMaxGroups + 1) * 4 + 8; }
 
   int32_t* off;   // [G+1] group row offsets
@@ -92,5 +93,7 @@ struct GroupSched {
     return c;
   }
 };
+
+using GroupSched = GroupSchedT<1024>;
 
 }  // namespace cti
