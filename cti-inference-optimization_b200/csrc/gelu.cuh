@@ -7,8 +7,8 @@
 // Q(u) = log2(erfcx(u/sqrt2)) and erfcx(z) = exp(z^2) erfc(z).  Q is smooth
 // and slowly varying, so a degree-10 polynomial (a Chebyshev least-squares
 // fit on [0, 8], converted to monomials by gelu_fit.py) evaluates it with
-// ten fused multiply-adds; one ex2 finishes erfc.  Phi = 1 - erfc/2 for
-// x >= 0 and erfc/2 for x < 0.  Past u = 8, erfc(u/sqrt2) < 1.3e-15, so u is
+// ten fused multiply-adds; one ex2 finishes erfc; then
+// GELU(x) = max(x, 0) - |x| * erfc(|x|/sqrt2)/2.  Past u = 8, erfc(u/sqrt2) < 1.3e-15, so u is
 // clamped inside Q only.
 //
 // Pairs of values are evaluated with the packed fp32x2 FMA of sm_100, which
@@ -65,14 +65,12 @@ CTI_DEVICE float ex2_approx(float x) {
   return y;
 }
 
-CTI_DEVICE float copysign_bits(float mag, float sgn) {
-  return __uint_as_float((__float_as_uint(mag) & 0x7fffffffu) |
-                         (__float_as_uint(sgn) & 0x80000000u));
-}
-
 // In-place GELU of N values (N even), ordered so that the N/2 packed Horner
-// chains interleave: every step issues N/2 independent f32x2 FMAs.
-//   Phi(x) = 0.5 + sign(x) * (0.5 - erfc(|x|/sqrt2)/2)
+// chains interleave: every step issues N/2 independent f32x2 FMAs.  Uses
+//   GELU(x) = max(x, 0) - |x| * erfc(|x|/sqrt2)/2,
+// which is exact on both sides (no 1 - Phi cancellation for x << 0); the
+// factor 1/2 is folded into the constant term (log2(1/2) = -1).
+// Infinite inputs give NaN.
 template <int N>
 CTI_DEVICE void gelu_n(float (&v)[N]) {
   using namespace gelu_detail;
@@ -83,7 +81,7 @@ CTI_DEVICE void gelu_n(float (&v)[N]) {
     uc[p] = f2_pack(fminf(fabsf(v[2 * p]), kU0), fminf(fabsf(v[2 * p + 1]), kU0));
     acc[p] = f2_pack(C10, C10);
   }
-  const float coef[10] = {C9, C8, C7, C6, C5, C4, C3, C2, C1, C0};
+  const float coef[10] = {C9, C8, C7, C6, C5, C4, C3, C2, C1, C0 - 1.0f};
 #pragma unroll
   for (int k = 0; k < 10; ++k) {
     const uint64_t ck = f2_pack(coef[k], coef[k]);
@@ -91,21 +89,15 @@ CTI_DEVICE void gelu_n(float (&v)[N]) {
     for (int p = 0; p < P; ++p) acc[p] = f2_fma(acc[p], uc[p], ck);
   }
   const uint64_t neg_half_log2e = f2_pack(kNegHalfLog2e, kNegHalfLog2e);
-  const uint64_t m_half = f2_pack(-0.5f, -0.5f);
-  const uint64_t half = f2_pack(0.5f, 0.5f);
 #pragma unroll
   for (int p = 0; p < P; ++p) {
     const uint64_t x = f2_pack(v[2 * p], v[2 * p + 1]);
     const uint64_t q = f2_fma(f2_mul(x, x), neg_half_log2e, acc[p]);
     float q0, q1;
     f2_unpack(q, q0, q1);
-    // t = 0.5 - erfc/2 (>= 0); Phi = 0.5 + copysign(t, x).
-    const uint64_t t = f2_fma(f2_pack(ex2_approx(q0), ex2_approx(q1)), m_half, half);
-    float t0, t1;
-    f2_unpack(t, t0, t1);
-    const uint64_t phi =
-        f2_add(f2_pack(copysign_bits(t0, v[2 * p]), copysign_bits(t1, v[2 * p + 1])), half);
-    f2_unpack(f2_mul(x, phi), v[2 * p], v[2 * p + 1]);
+    const float h0 = ex2_approx(q0), h1 = ex2_approx(q1);  // erfc(|x|/sqrt2)/2
+    v[2 * p] = fmaf(-fabsf(v[2 * p]), h0, fmaxf(v[2 * p], 0.0f));
+    v[2 * p + 1] = fmaf(-fabsf(v[2 * p + 1]), h1, fmaxf(v[2 * p + 1], 0.0f));
   }
 }
 

@@ -83,12 +83,13 @@ def test_fused_ffn_agrees_with_two_gemms(cuda_device):
 
 def test_gelu_epilogue_accuracy(cuda_device):
     """GELU of the epilogue vs the exact erf GELU (fp64): a GEMM with an
-    identity weight block returns gelu(x + b) rounded to bf16, which must be
-    the correctly rounded value up to one bf16 ulp."""
+    identity weight block returns gelu(x) rounded to bf16.  On [-8, 8] that
+    must be within one bf16 ulp of the exact value (relative 2^-7); beyond,
+    where |GELU(x) - max(x, 0)| < 1e-14, within 1e-12 absolute."""
     from cti_b200 import _lib, ops
 
     dev = cuda_device
-    xs = torch.linspace(-8.0, 8.0, 128 * 64 * 8).reshape(-1, 64)
+    xs = torch.linspace(-12.0, 12.0, 128 * 64 * 8).reshape(-1, 64)
     a = xs.bfloat16()
     w = torch.zeros(1, 128, 64)
     w[0, :64, :64] = torch.eye(64)
@@ -99,6 +100,8 @@ def test_gelu_epilogue_accuracy(cuda_device):
     xa = a.double()
     exact = xa * 0.5 * torch.special.erfc(-xa / 2 ** 0.5)
     got = out[:, :64].double().cpu()
-    ulp = exact.abs().clamp_min(1e-30) * 2.0 ** -7
-    assert ((got - exact).abs() <= ulp + 1e-30).all()
+    err = (got - exact).abs()
+    inner = xa.abs() <= 8
+    assert (err[inner] <= exact[inner].abs() * 2.0 ** -7 + 1e-30).all(), err[inner].max()
+    assert (err[~inner] <= 1e-12 + exact[~inner].abs() * 2.0 ** -7).all()
     assert torch.equal(out[:, :64].cpu(), out[:, 64:].cpu())
