@@ -14,8 +14,8 @@
 //   epilogue: acc1 -> +b1 -> GELU -> bf16 -> H[c%2] (shared memory, laid out
 //             exactly as a TMA 128-byte-swizzled K-major tile)
 //   GEMM2(c): acc2 (TMEM, D cols) += H[c%2] @ W2[e][:, c*128:+128]^T
-// The MMA thread issues GEMM1(c+1) before GEMM2(c), so the tensor core works
-// on the next chunk while the epilogue warps run the GELU of this one.
+// The MMA thread issues GEMM2(c) only after GEMM1(c+2), so the tensor core
+// works on other chunks while the epilogue warps run the GELU of chunk c.
 // After the last chunk, acc2 + b2 is written to Y as bf16.
 //
 // Roles (576 threads): warp 0 TMA producer (X tile once per tile; W1/W2
@@ -46,6 +46,10 @@ using Sched = GroupSchedT<256>;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr uint32_t kAcc1Col = 256;
+// GEMM2 of chunk c is issued after GEMM1 of chunk c+kLag: between the end of
+// GEMM1(c) and the start of GEMM2(c) the tensor core has 2*kLag GEMMs of other
+// chunks to run, which is the time the epilogue has for the GELU of chunk c.
+constexpr int kLag = 2;
 
 template <int D>
 struct FF {
@@ -178,13 +182,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < P::XK; ++kb)
           tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
         ++x_issued;
-        for (int s = 0; s <= nch && ok; ++s) {
+        for (int s = 0; s < nch + kLag && ok; ++s) {
           if (s < nch) {
             for (int kb = 0; kb < P::XK && ok; ++kb)
               ok = load_slab(&tmW1, kb * kBK, gw * F + s * kFC);
           }
-          if (s >= 1) {
-            const int c = s - 1;
+          if (s >= kLag) {
+            const int c = s - kLag;
             for (int kb = 0; kb < 2 && ok; ++kb)
               for (int hf = 0; hf < P::HALVES && ok; ++hf)
                 ok = load_slab(&tmW2, c * kFC + kb * kBK, gw * D + hf * 128);
@@ -212,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         if (!mbar_wait(x_full, (uint32_t)(it & 1), status, 0x205, abort_flag)) break;
         tc_fence_after();
-        for (int s = 0; s <= nch && ok; ++s) {
+        for (int s = 0; s < nch + kLag && ok; ++s) {
           if (s < nch) {  // GEMM1(s)
             const int64_t gc = (int64_t)it * nch + s;
             const int b = (int)(gc & 1);
@@ -246,8 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(&a1_full[b]);
             if (s == nch - 1) umma_commit(x_empty);
           }
-          if (s >= 1) {  // GEMM2(s-1)
-            const int c = s - 1;
+          if (s >= kLag) {  // GEMM2(s-kLag)
+            const int c = s - kLag;
             const int64_t gc = (int64_t)it * nch + c;
             const int b = (int)(gc & 1);
             const uint32_t k = (uint32_t)(gc >> 1);
