@@ -31,7 +31,7 @@ ERROR_NAMES = {
 ACT_NONE, ACT_RELU, ACT_GELU = 0, 1, 2
 ACTIVATIONS = {"none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU}
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
-ROUTER_BLOCK_TOKENS = 128
+ROUTER_BLOCK_TOKENS = 256
 MAX_EXPERTS = 128
 
 _P = ctypes.c_void_p

@@ -11,9 +11,9 @@
 // Per tile (128 token rows of one expert), d_ff is processed in 128-wide
 // chunks c:
 //   GEMM1(c): acc1[c%2] (TMEM, 128 cols) = X[128, D] @ W1[e][c*128:+128, :]^T
-//   epilogue: acc1 -> +b1 -> GELU -> bf16 -> H[c%2] (shared memory, laid out
+//   epilogue: acc1 -> +b1 -> GELU -> bf16 -> H (shared memory, laid out
 //             exactly as a TMA 128-byte-swizzled K-major tile)
-//   GEMM2(c): acc2 (TMEM, D cols) += H[c%2] @ W2[e][:, c*128:+128]^T
+//   GEMM2(c): acc2 (TMEM, D cols) += H @ W2[e][:, c*128:+128]^T
 // The MMA thread issues GEMM2(c) only after GEMM1(c+2), so the tensor core
 // works on other chunks while the epilogue warps run the GELU of chunk c.
 // After the last chunk, acc2 + b2 is written to Y as bf16.
@@ -26,8 +26,10 @@
 // staged in shared memory once per expert change).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
-// Shared memory (D=256): X 64 KB + H 2x32 KB + ring 5x16 KB + biases 5 KB +
-// scheduler 2 KB.  d_ff <= 1024 (one expert's b1 in shared memory).
+// Shared memory (D=256): X 64 KB + H 32 KB + ring 7x16 KB + biases 5 KB +
+// scheduler 2 KB.  One H buffer suffices with the two-chunk lag: the
+// epilogue writes H(c) after GEMM2(c-1) has read H(c-1), still well before
+// GEMM2(c) is due.  d_ff <= 1024 (one expert's b1 in shared memory).
 #include "common.cuh"
 #include "gelu.cuh"
 #include "sched.cuh"
@@ -55,9 +57,9 @@ template <int D>
 struct FF {
   static constexpr int XK = D / kBK;          // X k-slabs
   static constexpr int HALVES = D / 128;      // GEMM2 N halves of 128
-  static constexpr int STAGES = D == 256 ? 5 : 7;
+  static constexpr int STAGES = D == 256 ? 7 : 9;
   static constexpr size_t X_BYTES = (size_t)XK * kSlab;
-  static constexpr size_t H_BYTES = 2 * (size_t)2 * kSlab;  // two buffers of 128x128
+  static constexpr size_t H_BYTES = (size_t)2 * kSlab;  // one 128x128 hidden chunk
   static constexpr size_t RING_BYTES = (size_t)STAGES * kSlab;
   static constexpr size_t BIAS_BYTES = (size_t)(kMaxF + D) * 4;
   static constexpr size_t SMEM =
@@ -103,9 +105,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* x_empty = x_full + 1;
   uint64_t* a1_full = x_empty + 1;  // [2]
   uint64_t* a1_empty = a1_full + 2;  // [2]
-  uint64_t* h_full = a1_empty + 2;   // [2]
-  uint64_t* h_empty = h_full + 2;    // [2]
-  uint64_t* a2_full = h_empty + 2;
+  uint64_t* h_full = a1_empty + 2;
+  uint64_t* h_empty = h_full + 1;
+  uint64_t* a2_full = h_empty + 1;
   uint64_t* a2_empty = a2_full + 1;
   uint64_t* drain = a2_empty + 1;
   uint64_t* bfree = drain + 1;   // epilogue threads done with the staged biases
@@ -127,9 +129,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a1_full[i], 1);
       mbar_init(&a1_empty[i], kEpiThreads);
-      mbar_init(&h_full[i], kEpiThreads);
-      mbar_init(&h_empty[i], 1);
     }
+    mbar_init(h_full, kEpiThreads);
+    mbar_init(h_empty, 1);
     mbar_init(a2_full, 1);
     mbar_init(a2_empty, kEpiThreads);
     mbar_init(drain, 1);
@@ -253,15 +255,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s >= kLag) {  // GEMM2(s-kLag)
             const int c = s - kLag;
             const int64_t gc = (int64_t)it * nch + c;
-            const int b = (int)(gc & 1);
-            const uint32_t k = (uint32_t)(gc >> 1);
             if (c == 0) {
               if (!mbar_wait(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x208, abort_flag)) {
                 ok = false;
                 break;
               }
             }
-            if (!mbar_wait(&h_full[b], k & 1u, status, 0x209, abort_flag)) {
+            if (!mbar_wait(h_full, (uint32_t)(gc & 1), status, 0x209, abort_flag)) {
               ok = false;
               break;
             }
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = h_addr + (uint32_t)b * (2 * kSlab) + kb * kSlab;
+                const uint32_t a0 = h_addr + kb * kSlab;
                 const uint32_t b0 = ring_addr + stage * kSlab;
                 const uint32_t d = tmem_base + (uint32_t)hf * 128u;
 #pragma unroll
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             if (!ok) break;
-            umma_commit(&h_empty[b]);
+            umma_commit(h_empty);
             if (c == nch - 1) umma_commit(a2_full);
           }
         }
@@ -355,14 +355,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[8 * h + i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
         }
-        if (!mbar_wait(&h_empty[b], (k & 1u) ^ 1u, status, 0x20d, abort_flag)) {
+        if (!mbar_wait(h_empty, (uint32_t)(gc & 1) ^ 1u, status, 0x20d, abort_flag)) {
           ok = false;
           break;
         }
-        store_row32_swizzled(sh + (size_t)b * (2 * kSlab) + (size_t)(sub >> 1) * kSlab, r,
-                             (sub & 1) * 4, w);
+        store_row32_swizzled(sh + (size_t)(sub >> 1) * kSlab, r, (sub & 1) * 4, w);
         fence_proxy_async_smem();
-        mbar_arrive(&h_full[b]);
+        mbar_arrive(h_full);
       }
       if (!ok) break;
 

@@ -3,15 +3,15 @@
 // Restates TopKGate.forward (baseline/infer.py:298-309: logits = w_g(x),
 // softmax, topk(2)) and the fused_top2_gate_kernel of online_best/infer.py:
 // 1624-1778 (strict '>' scan, lower expert id wins a tie) for any E <= 128,
-// with fp32 weights.  One thread owns one token; its E logits live in
-// registers as E independent fused-multiply-add chains over d = 0..D-1 (the
+// with fp32 weights.  Each thread owns TPT tokens; their E logits live in
+// registers as independent fused-multiply-add chains over d = 0..D-1 (the
 // order the CPU restatement in oracle/router_order.c reproduces bit for bit).
-// Activations and router weights are staged through shared memory in
-// 32-wide d-slices: x is converted to fp32 and transposed so that the 32
-// lanes of a warp read 32 consecutive words, and the weight slice is stored
-// d-major so every lane reads the same float4 (a broadcast).
+// A thread streams its own token rows straight from HBM into registers,
+// 16 bytes at a time with the next load in flight (no shared-memory staging
+// and no barriers in the main loop); the router weights are staged once per
+// block in shared memory, d-major, so every lane reads the same float4.
 //
-// The block also produces the dispatch metadata: for each of its 128 tokens
+// The block also produces the dispatch metadata: for each of its 256 tokens
 // the rank of each route among the block's earlier routes to the same expert
 // (token order, k=0 before k=1), and the block's per-expert histogram.
 #include "common.cuh"
@@ -19,173 +19,191 @@
 namespace cti {
 namespace {
 
-constexpr int kTok = CTI_ROUTER_BLOCK_TOKENS;  // tokens (= threads) per block
-constexpr int kDs = 32;                        // d-slice staged per step
+constexpr int kTok = CTI_ROUTER_BLOCK_TOKENS;  // tokens per block
+constexpr int kWsFloats = 8192;                // 32 KB of staged router weights
 
-template <int EMAX>
-__global__ void __launch_bounds__(kTok) router_kernel(const __nv_bfloat16* __restrict__ x,
-                                                     const float* __restrict__ wg,
-                                                     const float* __restrict__ bg, int64_t T,
-                                                     int D, int E, int renorm,
-                                                     int32_t* __restrict__ idx2,
-                                                     float* __restrict__ gate2,
-                                                     int32_t* __restrict__ route_rank,
-                                                     int32_t* __restrict__ block_hist,
-                                                     int32_t* status) {
-  __shared__ float xs[kDs][kTok + 1];
-  __shared__ __align__(16) float ws[kDs][EMAX];
+template <int EMAX, int TPT>
+__global__ void __launch_bounds__(kTok / TPT) router_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ wg,
+    const float* __restrict__ bg, int64_t T, int D, int E, int renorm,
+    int32_t* __restrict__ idx2, float* __restrict__ gate2, int32_t* __restrict__ route_rank,
+    int32_t* __restrict__ block_hist) {
+  constexpr int NT = kTok / TPT;           // threads per block
+  constexpr int DS = kWsFloats / EMAX;     // d-slab of staged weights
+  __shared__ __align__(16) float ws[DS][EMAX];
   __shared__ int cnt[EMAX];
 
   const int tid = threadIdx.x;
   const int64_t t0 = (int64_t)blockIdx.x * kTok;
-  const int64_t t = t0 + tid;
-  const bool valid = t < T;
+  int64_t tok[TPT];
+  bool valid[TPT];
+  const uint4* xr[TPT];
+#pragma unroll
+  for (int j = 0; j < TPT; ++j) {
+    tok[j] = t0 + j * NT + tid;
+    valid[j] = tok[j] < T;
+    xr[j] = reinterpret_cast<const uint4*>(x + (valid[j] ? tok[j] : 0) * D);
+  }
 
-  float acc[EMAX];
+  float acc[TPT][EMAX];
 #pragma unroll
-  for (int e = 0; e < EMAX; ++e) acc[e] = 0.0f;
+  for (int j = 0; j < TPT; ++j)
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e) acc[j][e] = 0.0f;
 
-  for (int d0 = 0; d0 < D; d0 += kDs) {
-    // Stage x[t0:t0+128, d0:d0+32] as fp32, transposed.  512 chunks of 8
-    // bf16 (16 bytes): chunk c covers token c/4, d-offset (c%4)*8.
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int c = tid + i * kTok;
-      const int tok = c >> 2;
-      const int part = (c & 3) * 8;
-      float v[8];
-      if (t0 + tok < T) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(x + (t0 + tok) * D + d0 + part);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(h[j]);
-          v[2 * j] = f.x;
-          v[2 * j + 1] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) xs[part + j][tok] = v[j];
-    }
-    // Stage wg[:, d0:d0+32] d-major; experts >= E read as zero.
-    for (int i = tid; i < kDs * EMAX; i += kTok) {
-      const int e = i / kDs;
-      const int dd = i % kDs;
+  for (int d0 = 0; d0 < D; d0 += DS) {
+    const int ds = min(DS, D - d0);
+    __syncthreads();
+    for (int i = tid; i < EMAX * ds; i += NT) {
+      const int e = i / ds;
+      const int dd = i - e * ds;
       ws[dd][e] = (e < E) ? wg[(int64_t)e * D + d0 + dd] : 0.0f;
     }
     __syncthreads();
-#pragma unroll 4
-    for (int dd = 0; dd < kDs; ++dd) {
-      const float xv = xs[dd][tid];
-      const float4* w4 = reinterpret_cast<const float4*>(&ws[dd][0]);
+    uint4 cur[TPT];
 #pragma unroll
-      for (int q = 0; q < EMAX / 4; ++q) {
-        const float4 w = w4[q];
-        acc[4 * q + 0] = fmaf(xv, w.x, acc[4 * q + 0]);
-        acc[4 * q + 1] = fmaf(xv, w.y, acc[4 * q + 1]);
-        acc[4 * q + 2] = fmaf(xv, w.z, acc[4 * q + 2]);
-        acc[4 * q + 3] = fmaf(xv, w.w, acc[4 * q + 3]);
+    for (int j = 0; j < TPT; ++j) cur[j] = valid[j] ? __ldg(xr[j] + d0 / 8) : make_uint4(0, 0, 0, 0);
+    for (int dd = 0; dd < ds; dd += 8) {
+      uint4 nxt[TPT];
+      const bool more = dd + 8 < ds;
+#pragma unroll
+      for (int j = 0; j < TPT; ++j)
+        nxt[j] = (valid[j] && more) ? __ldg(xr[j] + (d0 + dd + 8) / 8) : make_uint4(0, 0, 0, 0);
+      float xv[TPT][8];
+#pragma unroll
+      for (int j = 0; j < TPT; ++j) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[j]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 f = __bfloat1622float2(h[u]);
+          xv[j][2 * u] = f.x;
+          xv[j][2 * u + 1] = f.y;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4* w4 = reinterpret_cast<const float4*>(&ws[dd + u][0]);
+#pragma unroll
+        for (int q = 0; q < EMAX / 4; ++q) {
+          const float4 w = w4[q];
+#pragma unroll
+          for (int j = 0; j < TPT; ++j) {
+            acc[j][4 * q + 0] = fmaf(xv[j][u], w.x, acc[j][4 * q + 0]);
+            acc[j][4 * q + 1] = fmaf(xv[j][u], w.y, acc[j][4 * q + 1]);
+            acc[j][4 * q + 2] = fmaf(xv[j][u], w.z, acc[j][4 * q + 2]);
+            acc[j][4 * q + 3] = fmaf(xv[j][u], w.w, acc[j][4 * q + 3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < TPT; ++j) cur[j] = nxt[j];
+    }
+  }
+
+  // Logits, then top-2 by a strict '>' scan in expert order (lower id wins).
+  int i1[TPT], i2[TPT];
+  float g1[TPT], g2[TPT];
+#pragma unroll
+  for (int j = 0; j < TPT; ++j) {
+    float best1 = 0.0f, best2 = 0.0f;
+    int a1 = 0, a2 = -1;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e) {
+      if (e < E) {
+        const float l = acc[j][e] + bg[e];
+        acc[j][e] = l;
+        if (e == 0) {
+          best1 = l;
+          a1 = 0;
+        } else if (l > best1) {
+          best2 = best1;
+          a2 = a1;
+          best1 = l;
+          a1 = e;
+        } else if (a2 < 0 || l > best2) {
+          best2 = l;
+          a2 = e;
+        }
       }
     }
-    __syncthreads();
-  }
-
-  // logits, then top-2 by a strict '>' scan in expert order (lower id wins).
-  float best1 = 0.0f, best2 = 0.0f;
-  int i1 = 0, i2 = -1;
+    if (renorm) {
+      // p1/(p1+p2) and p2/(p1+p2): the softmax denominator cancels.
+      const float r = expf(best2 - best1);
+      const float inv = 1.0f / (1.0f + r);
+      g1[j] = inv;
+      g2[j] = r * inv;
+    } else {
+      float sum = 0.0f;
 #pragma unroll
-  for (int e = 0; e < EMAX; ++e) {
-    if (e < E) {
-      const float l = acc[e] + bg[e];
-      acc[e] = l;
-      if (e == 0) {
-        best1 = l;
-        i1 = 0;
-      } else if (l > best1) {
-        best2 = best1;
-        i2 = i1;
-        best1 = l;
-        i1 = e;
-      } else if (i2 < 0 || l > best2) {
-        best2 = l;
-        i2 = e;
-      }
+      for (int e = 0; e < EMAX; ++e)
+        if (e < E) sum += expf(acc[j][e] - best1);
+      g1[j] = 1.0f / sum;
+      g2[j] = expf(best2 - best1) / sum;
     }
+    i1[j] = a1;
+    i2[j] = a2;
   }
 
-  float g1, g2;
-  if (renorm) {
-    // p1/(p1+p2) and p2/(p1+p2): the softmax denominator cancels.
-    const float r = expf(best2 - best1);
-    const float inv = 1.0f / (1.0f + r);
-    g1 = inv;
-    g2 = r * inv;
-  } else {
-    float s = 0.0f;
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E) s += expf(acc[e] - best1);
-    g1 = 1.0f / s;
-    g2 = expf(best2 - best1) / s;
-  }
-
-  // Block-level ranks and histogram.  Warps run one after the other so the
-  // ranks follow token order; inside a warp, routes are grouped by expert
-  // with ballots (one round per distinct expert present in the warp).
-  for (int e = tid; e < EMAX; e += kTok) cnt[e] = 0;
+  // Block-level ranks and histogram.  Token groups j, then warps, run one
+  // after the other so the ranks follow token order; inside a warp, routes
+  // are grouped by expert with ballots (one round per distinct expert).
+  for (int e = tid; e < EMAX; e += NT) cnt[e] = 0;
   __syncthreads();
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const unsigned lt = (1u << lane) - 1u;
-  int rank0 = 0, rank1 = 0;
-  for (int w = 0; w < kTok / 32; ++w) {
-    if (warp == w) {
-      bool done0 = !valid, done1 = !valid;
-      while (true) {
-        const unsigned p0 = __ballot_sync(0xffffffffu, !done0);
-        const unsigned p1 = __ballot_sync(0xffffffffu, !done1);
-        if ((p0 | p1) == 0u) break;
-        const int e = p0 ? __shfl_sync(0xffffffffu, i1, __ffs(p0) - 1)
-                         : __shfl_sync(0xffffffffu, i2, __ffs(p1) - 1);
-        const unsigned b0 = __ballot_sync(0xffffffffu, valid && i1 == e);
-        const unsigned b1 = __ballot_sync(0xffffffffu, valid && i2 == e);
-        const int base = cnt[e];
-        const int before = base + __popc(b0 & lt) + __popc(b1 & lt);
-        if (!done0 && i1 == e) {
-          rank0 = before;
-          done0 = true;
+  int rank0[TPT], rank1[TPT];
+#pragma unroll
+  for (int j = 0; j < TPT; ++j) {
+    rank0[j] = rank1[j] = 0;
+    for (int w = 0; w < NT / 32; ++w) {
+      if (warp == w) {
+        bool done0 = !valid[j], done1 = !valid[j];
+        while (true) {
+          const unsigned p0 = __ballot_sync(0xffffffffu, !done0);
+          const unsigned p1 = __ballot_sync(0xffffffffu, !done1);
+          if ((p0 | p1) == 0u) break;
+          const int e = p0 ? __shfl_sync(0xffffffffu, i1[j], __ffs(p0) - 1)
+                           : __shfl_sync(0xffffffffu, i2[j], __ffs(p1) - 1);
+          const unsigned b0 = __ballot_sync(0xffffffffu, valid[j] && i1[j] == e);
+          const unsigned b1 = __ballot_sync(0xffffffffu, valid[j] && i2[j] == e);
+          const int base = cnt[e];
+          const int before = base + __popc(b0 & lt) + __popc(b1 & lt);
+          if (!done0 && i1[j] == e) {
+            rank0[j] = before;
+            done0 = true;
+          }
+          if (!done1 && i2[j] == e) {
+            rank1[j] = before;
+            done1 = true;
+          }
+          __syncwarp();
+          if (lane == 0) cnt[e] = base + __popc(b0) + __popc(b1);
+          __syncwarp();
         }
-        if (!done1 && i2 == e) {
-          rank1 = before;
-          done1 = true;
-        }
-        __syncwarp();
-        if (lane == 0) cnt[e] = base + __popc(b0) + __popc(b1);
-        __syncwarp();
       }
+      __syncthreads();
     }
-    __syncthreads();
   }
 
-  if (valid) {
-    reinterpret_cast<int2*>(idx2)[t] = make_int2(i1, i2);
-    reinterpret_cast<float2*>(gate2)[t] = make_float2(g1, g2);
-    reinterpret_cast<int2*>(route_rank)[t] = make_int2(rank0, rank1);
+#pragma unroll
+  for (int j = 0; j < TPT; ++j) {
+    if (valid[j]) {
+      reinterpret_cast<int2*>(idx2)[tok[j]] = make_int2(i1[j], i2[j]);
+      reinterpret_cast<float2*>(gate2)[tok[j]] = make_float2(g1[j], g2[j]);
+      reinterpret_cast<int2*>(route_rank)[tok[j]] = make_int2(rank0[j], rank1[j]);
+    }
   }
-  for (int e = tid; e < E; e += kTok) block_hist[(int64_t)blockIdx.x * E + e] = cnt[e];
-  (void)status;
+  for (int e = tid; e < E; e += NT) block_hist[(int64_t)blockIdx.x * E + e] = cnt[e];
 }
 
-template <int EMAX>
+template <int EMAX, int TPT>
 cudaError_t launch_router(const __nv_bfloat16* x, const float* wg, const float* bg, int64_t T,
                           int D, int E, int renorm, int32_t* idx2, float* gate2, int32_t* rank,
-                          int32_t* hist, int32_t* status, cudaStream_t s) {
+                          int32_t* hist, cudaStream_t s) {
   const int64_t blocks = (T + kTok - 1) / kTok;
-  router_kernel<EMAX><<<(unsigned)blocks, kTok, 0, s>>>(x, wg, bg, T, D, E, renorm, idx2, gate2,
-                                                        rank, hist, status);
+  router_kernel<EMAX, TPT><<<(unsigned)blocks, kTok / TPT, 0, s>>>(x, wg, bg, T, D, E, renorm,
+                                                                   idx2, gate2, rank, hist);
   return cudaGetLastError();
 }
 
@@ -198,7 +216,7 @@ extern "C" int cti_moe_router(const void* x_bf16, const float* wg, const float* 
                               void* stream) {
   using namespace cti;
   if (T < 0 || D <= 0 || E < 2 || E > CTI_MAX_EXPERTS) return CTI_ERR_INVALID_ARG;
-  if (D % kDs != 0) return CTI_ERR_UNSUPPORTED;
+  if (D % 8 != 0) return CTI_ERR_UNSUPPORTED;
   if (T == 0) return CTI_OK;
   if (!x_bf16 || !wg || !bg || !idx2 || !gate2 || !route_rank || !block_hist)
     return CTI_ERR_INVALID_ARG;
@@ -208,20 +226,17 @@ extern "C" int cti_moe_router(const void* x_bf16, const float* wg, const float* 
   const auto* x = static_cast<const __nv_bfloat16*>(x_bf16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err;
+  (void)status;
   if (E <= 8)
-    err = launch_router<8>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist,
-                           status, s);
+    err = launch_router<8, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist, s);
   else if (E <= 16)
-    err = launch_router<16>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist,
-                            status, s);
+    err = launch_router<16, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist, s);
   else if (E <= 32)
-    err = launch_router<32>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist,
-                            status, s);
+    err = launch_router<32, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist, s);
   else if (E <= 64)
-    err = launch_router<64>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist,
-                            status, s);
+    err = launch_router<64, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist, s);
   else
-    err = launch_router<128>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist,
-                             status, s);
+    err = launch_router<128, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank, block_hist,
+                                s);
   return err == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
 }

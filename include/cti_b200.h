@@ -48,7 +48,7 @@ extern "C" {
 
 /* Tokens handled by one router block; the dispatch scratch holds one
  * E-wide histogram per block. */
-#define CTI_ROUTER_BLOCK_TOKENS 128
+#define CTI_ROUTER_BLOCK_TOKENS 256
 #define CTI_MAX_EXPERTS 128
 
 /* Library identity and device query. */
@@ -67,12 +67,12 @@ int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail, 
  *
  * logits[t,e] = bg[e] + sum_d x[t,d]*wg[e,d] in fp32 (x is bf16, wg/bg fp32);
  * the sum is one fused-multiply-add chain in increasing d.  Top-2 by logit
- * with ties to the lower expert id.  renorm=1: gates are the two softmax
+ * with ties to the lower expert id.  D % 8 == 0.  renorm=1: gates are the two softmax
  * probabilities renormalised to sum to 1; renorm=0: the raw softmax
  * probabilities (the reference's un-renormalised scores).
  * Outputs: idx2[T,2] int32, gate2[T,2] fp32, route_rank[T,2] int32 (rank of
- * each route among the same-expert routes of its 128-token block, token
- * order), block_hist[ceil(T/128), E] int32 (per-block expert counts; the
+ * each route among the same-expert routes of its 256-token block, token
+ * order), block_hist[ceil(T/256), E] int32 (per-block expert counts; the
  * dispatch scratch).  E <= 128.
  * ---------------------------------------------------------------------- */
 int cti_moe_router(const void* x_bf16, const float* wg, const float* bg, int64_t T, int D, int E,

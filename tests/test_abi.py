@@ -57,7 +57,7 @@ def test_argument_validation_needs_no_device():
     # E above the maximum, D not a multiple of 32, bad activation, bad shapes.
     assert lib.cti_moe_router(None, None, None, 16, 64, 200, 1, None, None, None, None, None,
                               None) == _lib.CTI_ERR_INVALID_ARG
-    assert lib.cti_moe_router(None, None, None, 16, 40, 8, 1, None, None, None, None, None,
+    assert lib.cti_moe_router(None, None, None, 16, 36, 8, 1, None, None, None, None, None,
                               None) == _lib.CTI_ERR_UNSUPPORTED
     assert lib.cti_moe_grouped_gemm(None, None, None, None, 1, 1, 16, 128, 64, 7, None, None,
                                     None) == _lib.CTI_ERR_INVALID_ARG
@@ -80,7 +80,7 @@ def test_workspace_queries():
     from cti_b200 import _lib
 
     lib = _lib.lib
-    assert lib.cti_moe_dispatch_workspace_bytes(69632, 16) == 544 * 16 * 4
+    assert lib.cti_moe_dispatch_workspace_bytes(69632, 16) == 272 * 16 * 4
     assert lib.cti_moe_dispatch_workspace_bytes(1, 8) == 8 * 4
     small = lib.cti_moe_layer_workspace_bytes(128, 256, 16, 1024)
     big = lib.cti_moe_layer_workspace_bytes(69632, 256, 16, 1024)

@@ -22,7 +22,8 @@ def _run(x_cpu, wg, bg, renorm, dev):
 
 @pytest.mark.parametrize("T,D,E", [(1, 128, 8), (255, 128, 8), (256, 128, 8), (257, 256, 16),
                                    (4096, 128, 8), (69632, 256, 16), (3000, 1024, 64),
-                                   (500, 64, 2), (700, 96, 128)])
+                                   (500, 64, 2), (700, 96, 128), (513, 40, 33),
+                                   (300, 2048, 16)])
 @pytest.mark.parametrize("renorm", [True, False])
 def test_router_bit_exact_vs_order_matched_oracle(cuda_device, T, D, E, renorm):
     g = torch.Generator().manual_seed(T + D + E)
@@ -69,7 +70,9 @@ def test_router_exact_ties_go_to_lower_expert_id(cuda_device):
 
 
 def test_router_block_metadata(cuda_device):
-    """block_hist counts every route of each 128-token block; route_rank is the
+    from cti_b200 import _lib
+
+    """block_hist counts every route of each 256-token block; route_rank is the
     route's position among the block's routes to the same expert."""
     g = torch.Generator().manual_seed(5)
     T, D, E = 1000, 128, 8
@@ -80,12 +83,13 @@ def test_router_block_metadata(cuda_device):
     idx = r.idx2.cpu().long()
     rank = r.route_rank.cpu().long()
     hist = r.block_hist.cpu().long()
-    for b in range((T + 127) // 128):
-        blk = idx[b * 128:(b + 1) * 128].reshape(-1)
+    B = _lib.ROUTER_BLOCK_TOKENS
+    for b in range((T + B - 1) // B):
+        blk = idx[b * B:(b + 1) * B].reshape(-1)
         assert torch.equal(hist[b], torch.bincount(blk, minlength=E))
         exp = torch.zeros_like(blk)
         seen = [0] * E
         for i, e in enumerate(blk.tolist()):
             exp[i] = seen[e]
             seen[e] += 1
-        assert torch.equal(rank[b * 128:(b + 1) * 128].reshape(-1), exp)
+        assert torch.equal(rank[b * B:(b + 1) * B].reshape(-1), exp)
