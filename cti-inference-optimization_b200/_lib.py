@@ -45,6 +45,7 @@ SIGNATURES = {
     "cti_num_sms": (_I, [_I, _P]),
     "cti_status_read": (_I, [_P, _I, _P, _P, _P]),
     "cti_moe_router": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "cti_moe_router_split": (_I, [_I, _I]),
     "cti_moe_dispatch_workspace_bytes": (_SZ, [_I64, _I]),
     "cti_moe_dispatch": (_I, [_P, _P, _P, _P, _I64, _I, _I, _P, _P, _P, _P, _P, _P]),
     "cti_moe_grouped_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I64, _I, _I, _I, _P, _P, _P]),

@@ -80,6 +80,14 @@ CTI_DEVICE void store_row32_swizzled(uint8_t* slab, int r, int j0, const uint32_
   }
 }
 
+// One arrival per warp: the lanes' prior writes are ordered before lane 0's
+// (release) arrive by the warp barrier.  Barriers signalled this way count
+// warps, not threads.
+CTI_DEVICE void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_ffn_kernel(const __grid_constant__ CUtensorMap tmX,
@@ -128,15 +136,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(x_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a1_full[i], 1);
-      mbar_init(&a1_empty[i], kEpiThreads);
+      mbar_init(&a1_empty[i], kEpiWarps);
     }
-    mbar_init(h_full, kEpiThreads);
+    mbar_init(h_full, kEpiWarps);
     mbar_init(h_empty, 1);
     mbar_init(a2_full, 1);
-    mbar_init(a2_empty, kEpiThreads);
+    mbar_init(a2_empty, kEpiWarps);
     mbar_init(drain, 1);
-    mbar_init(bfree, kEpiThreads);
-    mbar_init(bready, kEpiThreads);
+    mbar_init(bfree, kEpiWarps);
+    mbar_init(bready, kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -317,12 +325,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int gw = tc.g % Gw;
       if (gw != staged_gw) {  // the same decision in every epilogue thread
         if (n_staged > 0) {   // everyone is done with the previous expert's biases
-          mbar_arrive(bfree);
+          warp_arrive(bfree, lane);
           if (!mbar_wait(bfree, (n_staged - 1) & 1u, status, 0x20f, abort_flag)) break;
         }
         for (int i = etid; i < F; i += kEpiThreads) b1s[i] = b1[(int64_t)gw * F + i];
         for (int i = etid; i < D; i += kEpiThreads) b2s[i] = b2[(int64_t)gw * D + i];
-        mbar_arrive(bready);
+        warp_arrive(bready, lane);
         if (!mbar_wait(bready, n_staged & 1u, status, 0x210, abort_flag)) break;
         ++n_staged;
         staged_gw = gw;
@@ -342,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            v);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&a1_empty[b]);
+        warp_arrive(&a1_empty[b], lane);
 
         const float* bc = b1s + c * kFC + sub * 32;
         uint32_t w[16];
@@ -361,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         store_row32_swizzled(sh + (size_t)(sub >> 1) * kSlab, r, (sub & 1) * 4, w);
         fence_proxy_async_smem();
-        mbar_arrive(h_full);
+        warp_arrive(h_full, lane);
       }
       if (!ok) break;
 
@@ -379,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(a2_empty);
+      warp_arrive(a2_empty, lane);
       if (r < tc.rows) {
         const float* bo = b2s + sub * kOutCols;
         uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)tc.row0 + r) * D + sub * kOutCols);

@@ -65,8 +65,10 @@ int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail, 
  * 1800-1852) and the fused_top2_gate_kernel launch (online_best/infer.py:
  * 1624-1778, launched at :1818 and :2210).
  *
- * logits[t,e] = bg[e] + sum_d x[t,d]*wg[e,d] in fp32 (x is bf16, wg/bg fp32);
- * the sum is one fused-multiply-add chain in increasing d.  Top-2 by logit
+ * logits[t,e] = bg[e] + sum_d x[t,d]*wg[e,d] in fp32 (x is bf16, wg/bg fp32).
+ * The sum runs over S = cti_moe_router_split(D, E) contiguous d-parts, each
+ * one fused-multiply-add chain in increasing d from 0, combined as
+ * ((p0+p1)+(p2+p3)) (S=4), (p0+p1) (S=2) or p0 (S=1).  Top-2 by logit
  * with ties to the lower expert id.  D % 8 == 0.  renorm=1: gates are the two softmax
  * probabilities renormalised to sum to 1; renorm=0: the raw softmax
  * probabilities (the reference's un-renormalised scores).
@@ -78,6 +80,10 @@ int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail, 
 int cti_moe_router(const void* x_bf16, const float* wg, const float* bg, int64_t T, int D, int E,
                    int renorm, int32_t* idx2, float* gate2, int32_t* route_rank,
                    int32_t* block_hist, int32_t* status, void* stream);
+
+/* Number of d-parts S the router splits each logit sum into (1, 2 or 4);
+ * fixes the fp32 summation order documented above. */
+int cti_moe_router_split(int D, int E);
 
 /* Bytes of dispatch scratch (block_hist) for T tokens and E experts. */
 size_t cti_moe_dispatch_workspace_bytes(int64_t T, int E);
