@@ -9,7 +9,8 @@
 // d-range is cut into S contiguous parts (S = cti_moe_router_split(D, E));
 // part s is one fused-multiply-add chain over its d in increasing order,
 // starting from 0; the parts are combined as ((p0 + p1) + (p2 + p3)) for
-// S = 4, (p0 + p1) for S = 2; then the bias is added.
+// S = 4, (p0 + p1) for S = 2; then the bias is added.  The kernel uses
+// S <= 2 (S = 2 when E <= 64 and D % 16 == 0).
 //
 // Work split: S adjacent lanes share one token, each owning one part, so a
 // block of 256 tokens runs 256*S/TPT threads (TPT tokens per lane group).
@@ -30,10 +31,10 @@ namespace cti {
 namespace {
 
 constexpr int kTok = CTI_ROUTER_BLOCK_TOKENS;  // tokens per block
-constexpr int kWsFloats = 10240;               // 40 KB of staged router weights
+constexpr int kWsFloats = 6144;                // 24 KB of staged router weights
 
 int router_split(int D, int E) {
-  const int max_split = E <= 32 ? 4 : (E <= 64 ? 2 : 1);
+  const int max_split = E <= 64 ? 2 : 1;
   for (int s = max_split; s > 1; s >>= 1)
     if (D % (8 * s) == 0) return s;
   return 1;
@@ -243,6 +244,14 @@ cudaError_t launch_router(const __nv_bfloat16* x, const float* wg, const float* 
                           int D, int E, int renorm, int32_t* idx2, float* gate2, int32_t* rank,
                           int32_t* hist, cudaStream_t s) {
   const int64_t blocks = (T + kTok - 1) / kTok;
+  static bool attr_set = false;
+  if (!attr_set) {
+    // Two blocks per SM need more than the default shared-memory carveout.
+    cudaFuncSetAttribute(router_kernel<EMAX, TPT, S>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout,
+                         (int)cudaSharedmemCarveoutMaxShared);
+    attr_set = true;
+  }
   router_kernel<EMAX, TPT, S><<<(unsigned)blocks, kTok * S / TPT, 0, s>>>(
       x, wg, bg, T, D, E, renorm, idx2, gate2, rank, hist);
   return cudaGetLastError();
@@ -274,19 +283,21 @@ extern "C" int cti_moe_router(const void* x_bf16, const float* wg, const float* 
   cudaError_t err;
   (void)status;
   const int sp = router_split(D, E);
-#define CTI_ROUTER_CASE(EM, TP)                                                              \
-  (sp == 4   ? launch_router<EM, TP, 4>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,  \
-                                        block_hist, s)                                        \
-   : sp == 2 ? launch_router<EM, TP, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,  \
-                                        block_hist, s)                                        \
-             : launch_router<EM, TP, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,  \
-                                        block_hist, s))
   if (E <= 8)
-    err = CTI_ROUTER_CASE(8, 2);
+    err = sp == 2 ? launch_router<8, 1, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
+                                           block_hist, s)
+                  : launch_router<8, 1, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
+                                           block_hist, s);
   else if (E <= 16)
-    err = CTI_ROUTER_CASE(16, 2);
+    err = sp == 2 ? launch_router<16, 1, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
+                                            block_hist, s)
+                  : launch_router<16, 1, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
+                                            block_hist, s);
   else if (E <= 32)
-    err = CTI_ROUTER_CASE(32, 2);
+    err = sp == 2 ? launch_router<32, 1, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
+                                            block_hist, s)
+                  : launch_router<32, 1, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
+                                            block_hist, s);
   else if (E <= 64)
     err = sp == 2 ? launch_router<64, 1, 2>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
                                             block_hist, s)
@@ -295,6 +306,5 @@ extern "C" int cti_moe_router(const void* x_bf16, const float* wg, const float* 
   else
     err = launch_router<128, 1, 1>(x, wg, bg, T, D, E, renorm, idx2, gate2, route_rank,
                                    block_hist, s);
-#undef CTI_ROUTER_CASE
   return err == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
 }

@@ -25,7 +25,7 @@ static float bf16_to_f32(uint16_t h) {
 }
 
 int router_split(int D, int E) {
-  const int max_split = E <= 32 ? 4 : (E <= 64 ? 2 : 1);
+  const int max_split = E <= 64 ? 2 : 1;
   for (int s = max_split; s > 1; s >>= 1)
     if (D % (8 * s) == 0) return s;
   return 1;
