@@ -19,14 +19,15 @@
 // After the last chunk, acc2 + b2 is written to Y as bf16.
 //
 // Roles (576 threads): warp 0 TMA producer (X tile once per tile; W1/W2
-// 128x64 slices through a ring of 16 KB stages), warp 1 TMEM owner and MMA
-// issuer (tcgen05.mma M=128 N=128 K=16, bf16 -> fp32), warps 2-17 epilogue
+// slabs through a ring of 32 KB stages), warp 1 TMEM owner and MMA issuer
+// (tcgen05.mma M=128, K=16, bf16 -> fp32; N=128 for GEMM1, N=D for GEMM2),
+// warps 2-17 epilogue
 // (four warps per TMEM lane quadrant, each owning 32 of a chunk's 128
 // columns and a quarter of the output columns; the expert's biases are
 // staged in shared memory once per expert change).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
-// Shared memory (D=256): X 64 KB + H 32 KB + ring 7x16 KB + biases 5 KB +
+// Shared memory (D=256): X 64 KB + H 32 KB + ring 3x32 KB + biases 5 KB +
 // scheduler 2 KB.  One H buffer suffices with the two-chunk lag: the
 // epilogue writes H(c) after GEMM2(c-1) has read H(c-1), still well before
 // GEMM2(c) is due.  d_ff <= 1024 (one expert's b1 in shared memory).
@@ -42,6 +43,10 @@ constexpr int kBM = 128;
 constexpr int kFC = 128;           // d_ff chunk
 constexpr int kBK = 64;            // bf16 elements per 128-byte swizzled row
 constexpr int kSlab = kBM * kBK * 2;  // 16 KB: one 128x64 bf16 tile
+// Weight ring stages of 32 KB: each wait on a stage covers 8 MMAs (GEMM1,
+// N=128) or 4 MMAs of N=256 (GEMM2), enough tensor work to hide the cost of
+// the wait and fence on the issuing thread.
+constexpr int kStage = 2 * kSlab;
 constexpr int kEpiWarps = 16;
 constexpr int kMaxF = 1024;  // b1 of one expert staged in shared memory
 using Sched = GroupSchedT<256>;
@@ -56,11 +61,13 @@ constexpr int kLag = 2;
 template <int D>
 struct FF {
   static constexpr int XK = D / kBK;          // X k-slabs
-  static constexpr int HALVES = D / 128;      // GEMM2 N halves of 128
-  static constexpr int STAGES = D == 256 ? 7 : 9;
+  static constexpr int G1S = XK / 2;          // ring stages of W1 per chunk (2 k-slabs each)
+  static constexpr int KPS2 = kStage / (D * kBK * 2);  // W2 k-slabs [D x 64] per stage
+  static constexpr int G2S = 2 / KPS2;        // ring stages of W2 per chunk
+  static constexpr int STAGES = D == 256 ? 3 : 4;
   static constexpr size_t X_BYTES = (size_t)XK * kSlab;
   static constexpr size_t H_BYTES = (size_t)2 * kSlab;  // one 128x128 hidden chunk
-  static constexpr size_t RING_BYTES = (size_t)STAGES * kSlab;
+  static constexpr size_t RING_BYTES = (size_t)STAGES * kStage;
   static constexpr size_t BIAS_BYTES = (size_t)(kMaxF + D) * 4;
   static constexpr size_t SMEM =
       1024 + X_BYTES + H_BYTES + RING_BYTES + BIAS_BYTES + Sched::smem_bytes() + 256;
@@ -173,16 +180,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t issued = 0, x_issued = 0;
       int it = 0;
       bool ok = true;
-      auto load_slab = [&](const CUtensorMap* map, int c0, int c1) -> bool {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, status, 0x201, abort_flag)) return false;
-        mbar_arrive_expect_tx(&full[stage], kSlab);
-        tma_load_2d(ring + stage * kSlab, map, &full[stage], c0, c1);
+      // Claims the next ring stage (bounded wait) and arms it for kStage bytes.
+      auto acquire = [&]() -> uint8_t* {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, status, 0x201, abort_flag)) return nullptr;
+        mbar_arrive_expect_tx(&full[stage], kStage);
+        return ring + stage * kStage;
+      };
+      auto advance = [&]() {
         ++issued;
         if (++stage == P::STAGES) {
           stage = 0;
           phase ^= 1u;
         }
-        return true;
       };
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         const TileCoord tc = sched.decode(t);
@@ -193,15 +202,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
         ++x_issued;
         for (int s = 0; s < nch + kLag && ok; ++s) {
-          if (s < nch) {
-            for (int kb = 0; kb < P::XK && ok; ++kb)
-              ok = load_slab(&tmW1, kb * kBK, gw * F + s * kFC);
+          if (s < nch) {  // W1 rows [s*128, +128), two 64-wide k-slabs per stage
+            for (int j = 0; j < P::G1S && ok; ++j) {
+              uint8_t* buf = acquire();
+              if (!buf) {
+                ok = false;
+                break;
+              }
+              for (int h = 0; h < 2; ++h)
+                tma_load_2d(buf + h * kSlab, &tmW1, &full[stage], (2 * j + h) * kBK,
+                            gw * F + s * kFC);
+              advance();
+            }
           }
-          if (s >= kLag) {
+          if (s >= kLag && ok) {  // W2 [D rows, 64 k] slabs of chunk s-kLag
             const int c = s - kLag;
-            for (int kb = 0; kb < 2 && ok; ++kb)
-              for (int hf = 0; hf < P::HALVES && ok; ++hf)
-                ok = load_slab(&tmW2, c * kFC + kb * kBK, gw * D + hf * 128);
+            for (int j = 0; j < P::G2S && ok; ++j) {
+              uint8_t* buf = acquire();
+              if (!buf) {
+                ok = false;
+                break;
+              }
+              for (int h = 0; h < P::KPS2; ++h)
+                tma_load_2d(buf + h * (D * kBK * 2), &tmW2, &full[stage],
+                            c * kFC + (j * P::KPS2 + h) * kBK, gw * D);
+              advance();
+            }
           }
         }
       }
@@ -210,12 +236,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t n = issued - i;
         mbar_wait(&full[n % P::STAGES], (uint32_t)((n / P::STAGES) & 1), status, 0x203, nullptr);
       }
+      (void)kSlab;
       if (x_issued > 0) mbar_wait(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x204, nullptr);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, 128);
+      const uint32_t idesc1 = idesc_bf16_f32(kBM, 128);  // GEMM1: N = d_ff chunk
+      const uint32_t idesc2 = idesc_bf16_f32(kBM, D);    // GEMM2: N = d_model
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -223,6 +251,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t x_addr = smem_u32(sx);
       const uint32_t h_addr = smem_u32(sh);
       const uint32_t ring_addr = smem_u32(ring);
+      auto advance = [&]() {
+        if (++stage == P::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      };
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         if (!mbar_wait(x_full, (uint32_t)(it & 1), status, 0x205, abort_flag)) break;
         tc_fence_after();
@@ -237,30 +271,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t d = tmem_base + kAcc1Col + (uint32_t)b * 128u;
-            for (int kb = 0; kb < P::XK; ++kb) {
+            for (int j = 0; j < P::G1S; ++j) {
               if (!mbar_wait(&full[stage], phase, status, 0x207, abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t a0 = x_addr + kb * kSlab;
-              const uint32_t b0 = ring_addr + stage * kSlab;
+              const uint32_t b0 = ring_addr + stage * kStage;
 #pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)
-                umma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                          (kb | kk) != 0 ? 1u : 0u);
+              for (int h = 0; h < 2; ++h) {
+                const int kb = 2 * j + h;
+                const uint32_t a0 = x_addr + kb * kSlab;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                  umma_bf16(d, smem_desc_sw128(a0 + kk * 32),
+                            smem_desc_sw128(b0 + h * kSlab + kk * 32), idesc1,
+                            (kb | kk) != 0 ? 1u : 0u);
+              }
               any = true;
               umma_commit(&empty[stage]);
-              if (++stage == P::STAGES) {
-                stage = 0;
-                phase ^= 1u;
-              }
+              advance();
             }
             if (!ok) break;
             umma_commit(&a1_full[b]);
             if (s == nch - 1) umma_commit(x_empty);
           }
-          if (s >= kLag) {  // GEMM2(s-kLag)
+          if (s >= kLag) {  // GEMM2(s-kLag), N = D in one instruction
             const int c = s - kLag;
             const int64_t gc = (int64_t)it * nch + c;
             if (c == 0) {
@@ -274,26 +310,25 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            for (int kb = 0; kb < 2 && ok; ++kb) {
-              for (int hf = 0; hf < P::HALVES; ++hf) {
-                if (!mbar_wait(&full[stage], phase, status, 0x20a, abort_flag)) {
-                  ok = false;
-                  break;
-                }
-                tc_fence_after();
+            for (int j = 0; j < P::G2S; ++j) {
+              if (!mbar_wait(&full[stage], phase, status, 0x20a, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t b0 = ring_addr + stage * kStage;
+#pragma unroll
+              for (int h = 0; h < P::KPS2; ++h) {
+                const int kb = j * P::KPS2 + h;
                 const uint32_t a0 = h_addr + kb * kSlab;
-                const uint32_t b0 = ring_addr + stage * kSlab;
-                const uint32_t d = tmem_base + (uint32_t)hf * 128u;
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
-                  umma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
-                            idesc, (c | kb | kk) != 0 ? 1u : 0u);
-                umma_commit(&empty[stage]);
-                if (++stage == P::STAGES) {
-                  stage = 0;
-                  phase ^= 1u;
-                }
+                  umma_bf16(tmem_base, smem_desc_sw128(a0 + kk * 32),
+                            smem_desc_sw128(b0 + h * (D * kBK * 2) + kk * 32), idesc2,
+                            (c | kb | kk) != 0 ? 1u : 0u);
               }
+              umma_commit(&empty[stage]);
+              advance();
             }
             if (!ok) break;
             umma_commit(h_empty);
@@ -424,7 +459,7 @@ int launch_fused(const void* Xp, const void* W1, const float* b1, const void* W2
   CUtensorMap tmX, tmW1, tmW2;
   if (!make_tmap_bf16_2d(&tmX, Xp, (uint64_t)rows_total, D, D, kBM, kBK) ||
       !make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, D, D, 128, kBK) ||
-      !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * D, (uint64_t)F, (uint64_t)F, 128, kBK))
+      !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * D, (uint64_t)F, (uint64_t)F, D, kBK))
     return CTI_ERR_INVALID_ARG;
   static bool attr_set = false;
   if (!attr_set) {
