@@ -31,7 +31,7 @@ ERROR_NAMES = {
 ACT_NONE, ACT_RELU, ACT_GELU = 0, 1, 2
 ACTIVATIONS = {"none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU}
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
-ROUTER_BLOCK_TOKENS = 256
+ROUTER_BLOCK_TOKENS = 128
 MAX_EXPERTS = 128
 
 _P = ctypes.c_void_p
@@ -45,7 +45,6 @@ SIGNATURES = {
     "cti_num_sms": (_I, [_I, _P]),
     "cti_status_read": (_I, [_P, _I, _P, _P, _P]),
     "cti_moe_router": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
-    "cti_moe_router_split": (_I, [_I, _I]),
     "cti_moe_dispatch_workspace_bytes": (_SZ, [_I64, _I]),
     "cti_moe_dispatch": (_I, [_P, _P, _P, _P, _I64, _I, _I, _P, _P, _P, _P, _P, _P]),
     "cti_moe_grouped_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I64, _I, _I, _I, _P, _P, _P]),

@@ -7,18 +7,18 @@
 //   1. dispatch_scan_kernel: one CTA turns the router's per-block expert
 //      histograms into expert offsets[E+1] and per-block base offsets (an
 //      exclusive prefix over blocks, then over experts).
-//   2. dispatch_scatter_kernel: one warp per token computes the sorted
-//      position of its two routes (block base + in-block rank from the
-//      router) and copies the token row to both positions with 16-byte
-//      vector loads/stores.
+//   2. dispatch_scatter_kernel: per block of 32 tokens, one thread per token
+//      computes the sorted position of its two routes (block base + in-block
+//      rank from the router), then the block copies the 32 rows to both
+//      positions with 16-byte vector loads/stores.
 // Routes of one expert come out in token order, exactly the order of the
 // reference's `nonzero()`.
 //
 // Combine restates `out_flat[token_idx] += expert_out * weight`
 // (baseline/infer.py:350-353) and moe_top2_reduce_kernel
-// (online_best/infer.py:1603-1621): one warp per token reads the token's two
-// expert-output rows, weights them by the gates in fp32 and writes one bf16
-// row.
+// (online_best/infer.py:1603-1621): per block of 32 tokens, the token's two
+// expert-output rows are weighted by the gates in fp32 and written as one
+// bf16 row, 16 bytes per load and store.
 #include "common.cuh"
 
 namespace cti {
@@ -77,80 +77,105 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
   }
 }
 
-// One warp per token.  D % 8 == 0 (16-byte chunks of 8 bf16).
+constexpr int kRowsPerBlock = 32;  // tokens per block in scatter / combine
+
+// Block of 256 threads per 32 tokens.  Phase 1: one thread per token reads
+// its expert ids, in-block ranks and block bases and computes the two sorted
+// positions.  Phase 2: the block copies the 32 rows as 16-byte chunks, every
+// thread with several independent loads in flight.  D % 8 == 0.
 __global__ void __launch_bounds__(256) dispatch_scatter_kernel(
     const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx2,
     const int32_t* __restrict__ route_rank, const int32_t* __restrict__ block_base, int64_t T,
     int D, int E, int32_t* __restrict__ perm_inv, int32_t* __restrict__ sorted_token,
     __nv_bfloat16* __restrict__ xperm, int32_t* status) {
-  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
+  __shared__ int2 pos_s[kRowsPerBlock];
+  const int64_t t0 = (int64_t)blockIdx.x * kRowsPerBlock;
   const int64_t R = 2 * T;
-  const int2 e = reinterpret_cast<const int2*>(idx2)[t];
-  const int2 rk = reinterpret_cast<const int2*>(route_rank)[t];
-  const int64_t blk = t / CTI_ROUTER_BLOCK_TOKENS;
-  if (e.x < 0 || e.x >= E || e.y < 0 || e.y >= E) {
-    if (lane == 0) raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
-    return;
+  if (threadIdx.x < kRowsPerBlock) {
+    const int64_t t = t0 + threadIdx.x;
+    int2 p = make_int2(-1, -1);
+    if (t < T) {
+      const int2 e = reinterpret_cast<const int2*>(idx2)[t];
+      const int2 rk = reinterpret_cast<const int2*>(route_rank)[t];
+      const int64_t blk = t / CTI_ROUTER_BLOCK_TOKENS;
+      if (e.x < 0 || e.x >= E || e.y < 0 || e.y >= E) {
+        raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
+      } else {
+        const int64_t p0 = (int64_t)block_base[blk * E + e.x] + rk.x;
+        const int64_t p1 = (int64_t)block_base[blk * E + e.y] + rk.y;
+        if (p0 < 0 || p0 >= R || p1 < 0 || p1 >= R) {
+          raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
+        } else {
+          p = make_int2((int)p0, (int)p1);
+          reinterpret_cast<int2*>(perm_inv)[t] = p;
+          sorted_token[p0] = (int32_t)t;
+          sorted_token[p1] = (int32_t)t;
+        }
+      }
+    }
+    pos_s[threadIdx.x] = p;
   }
-  const int64_t p0 = (int64_t)block_base[blk * E + e.x] + rk.x;
-  const int64_t p1 = (int64_t)block_base[blk * E + e.y] + rk.y;
-  if (p0 < 0 || p0 >= R || p1 < 0 || p1 >= R) {
-    if (lane == 0) raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
-    return;
-  }
-  if (lane == 0) {
-    reinterpret_cast<int2*>(perm_inv)[t] = make_int2((int)p0, (int)p1);
-    sorted_token[p0] = (int32_t)t;
-    sorted_token[p1] = (int32_t)t;
-  }
+  __syncthreads();
   if (xperm == nullptr) return;
-  const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
-  uint4* d0 = reinterpret_cast<uint4*>(xperm + p0 * D);
-  uint4* d1 = reinterpret_cast<uint4*>(xperm + p1 * D);
   const int nchunk = D / 8;
-  for (int c = lane; c < nchunk; c += 32) {
-    const uint4 v = __ldg(src + c);
-    d0[c] = v;
-    d1[c] = v;
+  for (int c = threadIdx.x; c < kRowsPerBlock * nchunk; c += blockDim.x) {
+    const int r = c / nchunk;
+    const int ch = c - r * nchunk;
+    const int2 p = pos_s[r];
+    if (p.x < 0) continue;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (t0 + r) * D) + ch);
+    reinterpret_cast<uint4*>(xperm + (int64_t)p.x * D)[ch] = v;
+    reinterpret_cast<uint4*>(xperm + (int64_t)p.y * D)[ch] = v;
   }
 }
 
-// One warp per token.
+// Same shape: phase 1 loads each token's two sorted positions and gates,
+// phase 2 combines the two expert rows chunk by chunk in fp32.
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ Y,
                                                      int64_t Y_rows,
                                                      const int32_t* __restrict__ perm_inv,
                                                      const float* __restrict__ gate2, int64_t T,
                                                      int D, __nv_bfloat16* __restrict__ out,
                                                      int32_t* status) {
-  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const int2 p = reinterpret_cast<const int2*>(perm_inv)[t];
-  const float2 g = reinterpret_cast<const float2*>(gate2)[t];
-  if (p.x < 0 || p.x >= Y_rows || p.y < 0 || p.y >= Y_rows) {
-    if (lane == 0) raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
-    return;
+  __shared__ int2 pos_s[kRowsPerBlock];
+  __shared__ float2 gate_s[kRowsPerBlock];
+  const int64_t t0 = (int64_t)blockIdx.x * kRowsPerBlock;
+  if (threadIdx.x < kRowsPerBlock) {
+    const int64_t t = t0 + threadIdx.x;
+    int2 p = make_int2(-1, -1);
+    float2 g = make_float2(0.0f, 0.0f);
+    if (t < T) {
+      p = reinterpret_cast<const int2*>(perm_inv)[t];
+      g = reinterpret_cast<const float2*>(gate2)[t];
+      if (p.x < 0 || p.x >= Y_rows || p.y < 0 || p.y >= Y_rows) {
+        raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
+        p = make_int2(-1, -1);
+      }
+    }
+    pos_s[threadIdx.x] = p;
+    gate_s[threadIdx.x] = g;
   }
-  const uint4* y0 = reinterpret_cast<const uint4*>(Y + (int64_t)p.x * D);
-  const uint4* y1 = reinterpret_cast<const uint4*>(Y + (int64_t)p.y * D);
-  uint4* o = reinterpret_cast<uint4*>(out + t * D);
+  __syncthreads();
   const int nchunk = D / 8;
-  for (int c = lane; c < nchunk; c += 32) {
-    const uint4 a = __ldg(y0 + c);
-    const uint4 b = __ldg(y1 + c);
+  for (int c = threadIdx.x; c < kRowsPerBlock * nchunk; c += blockDim.x) {
+    const int r = c / nchunk;
+    const int ch = c - r * nchunk;
+    const int2 p = pos_s[r];
+    if (p.x < 0) continue;
+    const float2 g = gate_s[r];
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(Y + (int64_t)p.x * D) + ch);
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(Y + (int64_t)p.y * D) + ch);
     const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
     const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
-    uint4 r;
-    uint32_t* rw = reinterpret_cast<uint32_t*>(&r);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 fa = __bfloat1622float2(ha[j]);
       const float2 fb = __bfloat1622float2(hb[j]);
-      rw[j] = pack_bf16x2(fmaf(g.y, fb.x, g.x * fa.x), fmaf(g.y, fb.y, g.x * fa.y));
+      ow[j] = pack_bf16x2(fmaf(g.y, fb.x, g.x * fa.x), fmaf(g.y, fb.y, g.x * fa.y));
     }
-    o[c] = r;
+    reinterpret_cast<uint4*>(out + (t0 + r) * D)[ch] = o;
   }
 }
 
@@ -192,7 +217,7 @@ extern "C" int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const i
   const int64_t nblk = (T + CTI_ROUTER_BLOCK_TOKENS - 1) / CTI_ROUTER_BLOCK_TOKENS;
   dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(block_hist, nblk, E, offsets);
   if (cudaGetLastError() != cudaSuccess) return CTI_ERR_CUDA;
-  const int64_t blocks = (T + 7) / 8;
+  const int64_t blocks = (T + kRowsPerBlock - 1) / kRowsPerBlock;
   dispatch_scatter_kernel<<<(unsigned)blocks, 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(x_bf16), idx2, route_rank, block_hist, T, D, E, perm_inv,
       sorted_token, static_cast<__nv_bfloat16*>(xperm_bf16), status);
@@ -211,7 +236,7 @@ extern "C" int cti_moe_combine(const void* Y_bf16, int64_t Y_rows, const int32_t
       misaligned(gate2, 8))
     return CTI_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t blocks = (T + 7) / 8;
+  const int64_t blocks = (T + kRowsPerBlock - 1) / kRowsPerBlock;
   combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(Y_bf16),
                                                   Y_rows, perm_inv, gate2, T, D,
                                                   static_cast<__nv_bfloat16*>(out_bf16), status);

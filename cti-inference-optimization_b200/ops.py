@@ -19,7 +19,7 @@ from ._lib import check, lib, ptr, require_cuda, stream_handle, status_word
 class RouterOut:
     idx2: torch.Tensor  # [T, 2] int32 expert ids (top-1, top-2)
     gate2: torch.Tensor  # [T, 2] fp32 gate weights
-    route_rank: torch.Tensor  # [T, 2] int32 rank inside the 256-token router block
+    route_rank: torch.Tensor  # [T, 2] int32 rank inside the 128-token router block
     block_hist: torch.Tensor  # [ceil(T/128), E] int32 per-block expert counts
 
 

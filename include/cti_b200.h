@@ -48,7 +48,7 @@ extern "C" {
 
 /* Tokens handled by one router block; the dispatch scratch holds one
  * E-wide histogram per block. */
-#define CTI_ROUTER_BLOCK_TOKENS 256
+#define CTI_ROUTER_BLOCK_TOKENS 128
 #define CTI_MAX_EXPERTS 128
 
 /* Library identity and device query. */
@@ -65,25 +65,20 @@ int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail, 
  * 1800-1852) and the fused_top2_gate_kernel launch (online_best/infer.py:
  * 1624-1778, launched at :1818 and :2210).
  *
- * logits[t,e] = bg[e] + sum_d x[t,d]*wg[e,d] in fp32 (x is bf16, wg/bg fp32).
- * The sum runs over S = cti_moe_router_split(D, E) contiguous d-parts, each
- * one fused-multiply-add chain in increasing d from 0, combined as
- * ((p0+p1)+(p2+p3)) (S=4), (p0+p1) (S=2) or p0 (S=1).  Top-2 by logit
+ * logits[t,e] = bg[e] + sum_d x[t,d]*wg[e,d] in fp32 (x is bf16, wg/bg fp32);
+ * the sum is one fused-multiply-add chain in increasing d from 0, and the
+ * bias is added after it.  Top-2 by logit
  * with ties to the lower expert id.  D % 8 == 0.  renorm=1: gates are the two softmax
  * probabilities renormalised to sum to 1; renorm=0: the raw softmax
  * probabilities (the reference's un-renormalised scores).
  * Outputs: idx2[T,2] int32, gate2[T,2] fp32, route_rank[T,2] int32 (rank of
- * each route among the same-expert routes of its 256-token block, token
- * order), block_hist[ceil(T/256), E] int32 (per-block expert counts; the
+ * each route among the same-expert routes of its 128-token block, token
+ * order), block_hist[ceil(T/128), E] int32 (per-block expert counts; the
  * dispatch scratch).  E <= 128.
  * ---------------------------------------------------------------------- */
 int cti_moe_router(const void* x_bf16, const float* wg, const float* bg, int64_t T, int D, int E,
                    int renorm, int32_t* idx2, float* gate2, int32_t* route_rank,
                    int32_t* block_hist, int32_t* status, void* stream);
-
-/* Number of d-parts S the router splits each logit sum into (1, 2 or 4);
- * fixes the fp32 summation order documented above. */
-int cti_moe_router_split(int D, int E);
 
 /* Bytes of dispatch scratch (block_hist) for T tokens and E experts. */
 size_t cti_moe_dispatch_workspace_bytes(int64_t T, int E);

@@ -48,11 +48,5 @@ def router_order(x_bf16_u16: np.ndarray, wg: np.ndarray, bg: np.ndarray, renorm:
     return idx2, gate2, logits
 
 
-def router_split(D: int, E: int) -> int:
-    lib = ctypes.CDLL(str(build()))
-    lib.router_split.argtypes = [ctypes.c_int, ctypes.c_int]
-    return int(lib.router_split(D, E))
-
-
 if __name__ == "__main__":
     print(build(force=True))
