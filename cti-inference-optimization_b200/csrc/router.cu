@@ -70,47 +70,70 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
+  // x chunks are prefetched into registers one step ahead: chunk c of a
+  // d-step is token c % 128, 8-wide d-part c / 128 (consecutive lanes store
+  // consecutive tokens in shared memory).
+  constexpr int kXChunks = kTok * (kDC / 8);                   // 512 per step
+  constexpr int kXPerThread = (kXChunks + NT - 1) / NT;
+  uint4 xpre[kXPerThread];
+  auto load_x = [&](int d0) {
+    const int dc = min(kDC, D - d0);
+#pragma unroll
+    for (int q = 0; q < kXPerThread; ++q) {
+      const int c = tid + q * NT;
+      const int tok = c % kTok;
+      const int part = c / kTok;
+      xpre[q] = (c < kXChunks && part * 8 < dc && t0 + tok < T)
+                    ? __ldg(reinterpret_cast<const uint4*>(x + (t0 + tok) * D + d0) + part)
+                    : make_uint4(0, 0, 0, 0);
+    }
+  };
+  load_x(0);
   for (int d0 = 0; d0 < D; d0 += kDC) {
     const int dc = min(kDC, D - d0);  // a multiple of 8
     __syncthreads();
-    // x[t0:t0+128, d0:d0+dc] -> xs[dd][t] as fp32.  Chunk c: token c % 128,
-    // 8-wide d-part c / 128, so consecutive lanes store consecutive tokens.
-    for (int c = tid; c < kTok * (dc / 8); c += NT) {
-      const int tok = c % kTok;
-      const int part = c / kTok;
-      float v[8];
-      if (t0 + tok < T) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + (t0 + tok) * D + d0) + part);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int q = 0; q < kXPerThread; ++q) {
+      const int c = tid + q * NT;
+      if (c < kXChunks) {
+        const int tok = c % kTok;
+        const int part = c / kTok;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xpre[q]);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const float2 f = __bfloat1622float2(h[u]);
-          v[2 * u] = f.x;
-          v[2 * u + 1] = f.y;
+          xs[part * 8 + 2 * u][tok] = f.x;
+          xs[part * 8 + 2 * u + 1][tok] = f.y;
         }
-      } else {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = 0.0f;
       }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) xs[part * 8 + u][tok] = v[u];
     }
-    for (int i = tid; i < EMAX * dc; i += NT) {
-      const int e = i / dc;
-      const int dd = i - e * dc;
-      ws[dd][e] = (e < E) ? wg[(int64_t)e * D + d0 + dd] : 0.0f;
+    // ws[dd][e] = wg[e][d0 + dd]; i = e * kDC + dd keeps the global reads
+    // coalesced along d.
+    for (int i = tid; i < EMAX * kDC; i += NT) {
+      const int e = i / kDC;
+      const int dd = i % kDC;
+      ws[dd][e] = (e < E && dd < dc) ? wg[(int64_t)e * D + d0 + dd] : 0.0f;
     }
     __syncthreads();
+    if (d0 + kDC < D) load_x(d0 + kDC);  // in flight during this step's FMAs
+    if (gemm) {
+      float4 xv = *reinterpret_cast<const float4*>(&xs[0][4 * tg]);
+      float4 wv = *reinterpret_cast<const float4*>(&ws[0][4 * eg]);
 #pragma unroll 8
-    for (int dd = 0; dd < (gemm ? dc : 0); ++dd) {
-      const float4 xv = *reinterpret_cast<const float4*>(&xs[dd][4 * tg]);
-      const float4 wv = *reinterpret_cast<const float4*>(&ws[dd][4 * eg]);
-      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-      const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+      for (int dd = 0; dd < dc; ++dd) {
+        // Operands of step dd+1 are loaded before the FMAs of step dd.
+        const int nd = dd + 1 < dc ? dd + 1 : dd;
+        const float4 xn = *reinterpret_cast<const float4*>(&xs[nd][4 * tg]);
+        const float4 wn = *reinterpret_cast<const float4*>(&ws[nd][4 * eg]);
+        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+        const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+        xv = xn;
+        wv = wn;
+      }
     }
   }
   __syncthreads();  // xs/ws are about to be overwritten by lg
