@@ -14,8 +14,9 @@
 // tile (16 independent chains) and, per d, reads one float4 of activations
 // and one float4 of weights from shared memory - two conflict-free loads per
 // 16 FMAs, so the kernel is bound by the FMA pipe rather than by shared
-// memory.  Activations are staged 32 d at a time, converted to fp32 and
-// stored d-major; router weights are staged alongside.
+// memory.  Activations and router weights are staged 32 d at a time
+// (activations converted to fp32, both d-major), and the global loads of the
+// next step are in flight while the current step's FMAs run.
 //
 // The block also produces the dispatch metadata: for each of its 128 tokens
 // the rank of each route among the block's earlier routes to the same expert
@@ -33,7 +34,7 @@ struct RouterSmem {
   static constexpr int kStage = kDC * kTok + kDC * EMAX;
   static constexpr int kLogits = kTok * (EMAX + 1);
   static constexpr int kFloats = kStage > kLogits ? kStage : kLogits;
-  static constexpr size_t kBytes = (size_t)kFloats * 4 + EMAX * 4;
+  static constexpr size_t kBytes = (size_t)kFloats * 4 + (size_t)(1 + kTok / 32) * EMAX * 4;
 };
 
 template <int EMAX>
@@ -51,7 +52,8 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
   constexpr int NG = 32 * EG;        // GEMM threads: 32 token groups x EG expert groups
   constexpr int NT = NG < kTok ? kTok : NG;  // at least one thread per token
   // Dynamic shared memory: xs[kDC][kTok] and ws[kDC][EMAX] while the
-  // logits are accumulated, then reused as lg[kTok][EMAX + 1]; cnt[EMAX] last.
+  // logits are accumulated, then reused as lg[kTok][EMAX + 1]; then cnt[EMAX]
+  // (block counts) and the per-warp counts [kTok/32][EMAX].
   extern __shared__ __align__(16) float smem_f[];
   float (*xs)[kTok] = reinterpret_cast<float (*)[kTok]>(smem_f);
   float (*ws)[EMAX] = reinterpret_cast<float (*)[EMAX]>(smem_f + kDC * kTok);
@@ -75,8 +77,11 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
   // consecutive tokens in shared memory).
   constexpr int kXChunks = kTok * (kDC / 8);                   // 512 per step
   constexpr int kXPerThread = (kXChunks + NT - 1) / NT;
+  constexpr int kWChunks = EMAX * (kDC / 4);                   // float4s of wg per step
+  constexpr int kWPerThread = (kWChunks + NT - 1) / NT;
   uint4 xpre[kXPerThread];
-  auto load_x = [&](int d0) {
+  float4 wpre[kWPerThread];
+  auto load_step = [&](int d0) {
     const int dc = min(kDC, D - d0);
 #pragma unroll
     for (int q = 0; q < kXPerThread; ++q) {
@@ -87,8 +92,18 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
                     ? __ldg(reinterpret_cast<const uint4*>(x + (t0 + tok) * D + d0) + part)
                     : make_uint4(0, 0, 0, 0);
     }
+    // wg[e][d0 + 4*j .. +3] for chunk c = e * (kDC/4) + j (coalesced along d).
+#pragma unroll
+    for (int q = 0; q < kWPerThread; ++q) {
+      const int c = tid + q * NT;
+      const int e = c / (kDC / 4);
+      const int j = c % (kDC / 4);
+      wpre[q] = (c < kWChunks && e < E && 4 * j < dc)
+                    ? __ldg(reinterpret_cast<const float4*>(wg + (int64_t)e * D + d0) + j)
+                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
   };
-  load_x(0);
+  load_step(0);
   for (int d0 = 0; d0 < D; d0 += kDC) {
     const int dc = min(kDC, D - d0);  // a multiple of 8
     __syncthreads();
@@ -107,15 +122,20 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
         }
       }
     }
-    // ws[dd][e] = wg[e][d0 + dd]; i = e * kDC + dd keeps the global reads
-    // coalesced along d.
-    for (int i = tid; i < EMAX * kDC; i += NT) {
-      const int e = i / kDC;
-      const int dd = i % kDC;
-      ws[dd][e] = (e < E && dd < dc) ? wg[(int64_t)e * D + d0 + dd] : 0.0f;
+#pragma unroll
+    for (int q = 0; q < kWPerThread; ++q) {
+      const int c = tid + q * NT;
+      if (c < kWChunks) {
+        const int e = c / (kDC / 4);
+        const int j = c % (kDC / 4);
+        ws[4 * j + 0][e] = wpre[q].x;
+        ws[4 * j + 1][e] = wpre[q].y;
+        ws[4 * j + 2][e] = wpre[q].z;
+        ws[4 * j + 3][e] = wpre[q].w;
+      }
     }
     __syncthreads();
-    if (d0 + kDC < D) load_x(d0 + kDC);  // in flight during this step's FMAs
+    if (d0 + kDC < D) load_step(d0 + kDC);  // in flight during this step's FMAs
     if (gemm) {
       float4 xv = *reinterpret_cast<const float4*>(&xs[0][4 * tg]);
       float4 wv = *reinterpret_cast<const float4*>(&ws[0][4 * eg]);
@@ -143,7 +163,6 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
 #pragma unroll
       for (int j = 0; j < 4; ++j) lg[4 * tg + i][4 * eg + j] = acc[i][j];
   }
-  for (int e = tid; e < EMAX; e += NT) cnt[e] = 0;
   __syncthreads();
 
   // One thread per token: logits, top-2 by a strict '>' scan in expert order
@@ -185,40 +204,56 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
     }
   }
 
-  // Block-level ranks and histogram.  Warps run one after the other so the
-  // ranks follow token order; inside a warp, routes are grouped by expert
-  // with ballots (one round per distinct expert present in the warp).
+  // Block-level ranks and histogram.  Every warp ranks its 32 tokens' routes
+  // at once (routes grouped by expert with ballots, one round per distinct
+  // expert; k=0 before k=1 within a token) and records its own per-expert
+  // counts; then an exclusive prefix over the warps per expert turns the
+  // in-warp ranks into in-block ranks in token order.
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const unsigned lt = (1u << lane) - 1u;
+  int* wcnt = cnt + EMAX;  // [kTok / 32][EMAX] per-warp counts
+  for (int i = tid; i < (kTok / 32) * EMAX; i += NT) wcnt[i] = 0;
+  __syncthreads();
   int rank0 = 0, rank1 = 0;
-  for (int w = 0; w < kTok / 32; ++w) {
-    if (warp == w) {
-      bool done0 = !valid, done1 = !valid;
-      while (true) {
-        const unsigned p0 = __ballot_sync(0xffffffffu, !done0);
-        const unsigned p1 = __ballot_sync(0xffffffffu, !done1);
-        if ((p0 | p1) == 0u) break;
-        const int e = p0 ? __shfl_sync(0xffffffffu, i1, __ffs(p0) - 1)
-                         : __shfl_sync(0xffffffffu, i2, __ffs(p1) - 1);
-        const unsigned b0 = __ballot_sync(0xffffffffu, valid && i1 == e);
-        const unsigned b1 = __ballot_sync(0xffffffffu, valid && i2 == e);
-        const int base = cnt[e];
-        const int before = base + __popc(b0 & lt) + __popc(b1 & lt);
-        if (!done0 && i1 == e) {
-          rank0 = before;
-          done0 = true;
-        }
-        if (!done1 && i2 == e) {
-          rank1 = before;
-          done1 = true;
-        }
-        __syncwarp();
-        if (lane == 0) cnt[e] = base + __popc(b0) + __popc(b1);
-        __syncwarp();
+  if (warp < kTok / 32) {
+    bool done0 = !valid, done1 = !valid;
+    while (true) {
+      const unsigned p0 = __ballot_sync(0xffffffffu, !done0);
+      const unsigned p1 = __ballot_sync(0xffffffffu, !done1);
+      if ((p0 | p1) == 0u) break;
+      const int e = p0 ? __shfl_sync(0xffffffffu, i1, __ffs(p0) - 1)
+                       : __shfl_sync(0xffffffffu, i2, __ffs(p1) - 1);
+      const unsigned b0 = __ballot_sync(0xffffffffu, valid && i1 == e);
+      const unsigned b1 = __ballot_sync(0xffffffffu, valid && i2 == e);
+      const int before = __popc(b0 & lt) + __popc(b1 & lt);
+      if (!done0 && i1 == e) {
+        rank0 = before;
+        done0 = true;
       }
+      if (!done1 && i2 == e) {
+        rank1 = before;
+        done1 = true;
+      }
+      if (lane == 0) wcnt[warp * EMAX + e] = __popc(b0) + __popc(b1);
     }
-    __syncthreads();
+  }
+  __syncthreads();
+  // Exclusive prefix over warps, per expert; cnt[e] = block total.
+  for (int e = tid; e < EMAX; e += NT) {
+    int run = 0;
+#pragma unroll
+    for (int w = 0; w < kTok / 32; ++w) {
+      const int v = wcnt[w * EMAX + e];
+      wcnt[w * EMAX + e] = run;
+      run += v;
+    }
+    cnt[e] = run;
+  }
+  __syncthreads();
+  if (valid) {
+    rank0 += wcnt[warp * EMAX + i1];
+    rank1 += wcnt[warp * EMAX + i2];
   }
 
   if (valid) {
@@ -259,7 +294,8 @@ extern "C" int cti_moe_router(const void* x_bf16, const float* wg, const float* 
   if (T == 0) return CTI_OK;
   if (!x_bf16 || !wg || !bg || !idx2 || !gate2 || !route_rank || !block_hist)
     return CTI_ERR_INVALID_ARG;
-  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 || (reinterpret_cast<uintptr_t>(idx2) & 7) ||
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 || (reinterpret_cast<uintptr_t>(wg) & 15) ||
+      (reinterpret_cast<uintptr_t>(idx2) & 7) ||
       (reinterpret_cast<uintptr_t>(gate2) & 7) || (reinterpret_cast<uintptr_t>(route_rank) & 7))
     return CTI_ERR_INVALID_ARG;
   const auto* x = static_cast<const __nv_bfloat16*>(x_bf16);
