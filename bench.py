@@ -408,6 +408,17 @@ def run_profile_workload(args):
     from cti_b200 import _lib, ops, synth
 
     dev = torch.device("cuda", 0)
+    if args.profile == "embbag":
+        bb = synth.bag_batch(batch=4096, seed=0)
+        table = synth.embedding_table(bb.total_rows, 64, seed=0, device=dev)
+        a = [bb.values.to(dev), bb.row_offsets.to(dev), bb.val_offsets.to(dev), table,
+             bb.table_row_base.to(dev), bb.vocab.to(dev), bb.features]
+        for _ in range(args.warmup + args.steps):
+            ops.embedding_bag_sum(*a)
+        torch.cuda.synchronize(dev)
+        _lib.raise_on_status(dev)
+        print(f"profile workload embbag: {bb.values.numel()} ids")
+        return
     cfg = synth.CFG2
     T, _ = synth.moe_tokens(cfg)
     w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, device=dev)
@@ -434,6 +445,70 @@ def run_profile_workload(args):
     print(f"profile workload {args.profile}: T={T}, {args.warmup + args.steps} launches")
 
 
+def run_embbag(args, world, rank, local):
+    """--config cfg3: the 28-feature embedding-bag pooling (fp32 output),
+    metric = algorithmic GB/s; every rank pools its own batch."""
+    from cti_b200 import _lib, ops, synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    bb = synth.bag_batch(batch=4096, seed=rank)
+    table = synth.embedding_table(bb.total_rows, 64, seed=rank, device=dev)
+    a = [bb.values.to(dev), bb.row_offsets.to(dev), bb.val_offsets.to(dev), table,
+         bb.table_row_base.to(dev), bb.vocab.to(dev), bb.features]
+    out = torch.empty(bb.batch, bb.features * 64, dtype=torch.float32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    N = bb.values.numel()
+    byts = 8 * N + 8 * bb.features * (bb.batch + 1) + 128 * N + 4 * bb.batch * bb.features * 64
+    for _ in range(args.warmup):
+        ops.embedding_bag_sum(*a, out=out)
+    torch.cuda.synchronize(dev)
+    _lib.raise_on_status(dev)
+    barrier(world)
+    times = time_steps(lambda: ops.embedding_bag_sum(*a, out=out), args.steps, flush, dev)
+    barrier(world)
+    step_ms = max_over_ranks(statistics.median(times), world, dev)
+    value = sum_over_ranks(float(byts), world, dev) / (step_ms / 1e3) / 1e9
+    # end to end: pinned host ids/offsets -> device, pooling, pooled rows -> pinned host
+    host = [t.pin_memory() for t in (bb.values, bb.row_offsets, bb.val_offsets)]
+    dev_in = [torch.empty_like(t, device=dev) for t in host]
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e():
+        for d_, h_ in zip(dev_in, host):
+            d_.copy_(h_, non_blocking=True)
+        ops.embedding_bag_sum(dev_in[0], dev_in[1], dev_in[2], table, a[4], a[5], bb.features,
+                              out=out)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e()
+    e2e_ms = max_over_ranks(statistics.median(time_steps(e2e, args.steps, flush, dev,
+                                                         hide_host=False)), world, dev)
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    peaks, src = load_peaks()
+    if rank != 0:
+        return
+    line = {
+        "metric": "embedding_bag_GBps", "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16->f32",
+        "data": "synthetic",
+        "config": {"workload": "cfg3: 28-feature embedding-bag sum pooling, batch 4096, dim 64",
+                   "ids": N, "table_rows": bb.total_rows, "algorithmic_bytes": byts,
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "e2e": {"value": sum_over_ranks(float(byts), world, dev) / (e2e_ms / 1e3) / 1e9
+                if world == 1 else None, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * 4},
+        "roofline": {"bound": "hbm", "kernel": "embbag_kernel<64, float>",
+                     "achieved": value / world, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                     "frac": value / world / float(peaks["hbm_gbs"]),
+                     "peak_source": f"hbm_gbs of {src}", "traffic": None},
+        "gpu_launches": args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -442,8 +517,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3"],
+                    help="cfg2: MoE layer (default, the headline); cfg3: embedding bag")
     ap.add_argument("--profile", default=None,
-                    choices=["router", "dispatch", "ffn_fused", "ffn_fc1", "combine", "layer"],
+                    choices=["router", "dispatch", "ffn_fused", "ffn_fc1", "combine", "layer",
+                             "embbag"],
                     help="run one stage of the configuration-2 workload for an ncu capture")
     args = ap.parse_args()
     if args.profile:
@@ -457,7 +535,10 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        run_ours(args, world, rank, local)
+        if args.config == "cfg3":
+            run_embbag(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist
