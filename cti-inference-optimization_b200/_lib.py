@@ -33,6 +33,8 @@ ACTIVATIONS = {"none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU}
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 ROUTER_BLOCK_TOKENS = 128
 MAX_EXPERTS = 128
+NOALLOC_MAX_TOKENS = 131072
+NOALLOC_MAX_EXPERTS = 128
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -47,6 +49,8 @@ SIGNATURES = {
     "cti_moe_router": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "cti_moe_dispatch_workspace_bytes": (_SZ, [_I64, _I]),
     "cti_moe_dispatch": (_I, [_P, _P, _P, _P, _I64, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "cti_moe_route_dispatch_noalloc": (
+        _I, [_P, _P, _P, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "cti_moe_grouped_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I64, _I, _I, _I, _P, _P, _P]),
     "cti_moe_expert_ffn_fused": (
         _I,

@@ -103,6 +103,30 @@ int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const int32_t* rou
                      void* stream);
 
 /* ------------------------------------------------------------------------
+ * Routing + dispatch for callers that cannot allocate device memory.
+ * This entry point has no counterpart in the reference.
+ *
+ * Same results as cti_moe_router followed by cti_moe_dispatch (idx2, gate2,
+ * offsets, perm_inv, sorted_token, xperm), but the scratch those two need
+ * between them (route ranks and per-block expert counts) lives in a
+ * 1.5 MiB array inside the library instead of a caller workspace - for a
+ * host that binds only this C library and has no device allocator, or that
+ * must stay inside a fixed pre-reserved memory budget.  Limits: T <=
+ * CTI_NOALLOC_MAX_TOKENS, E <= CTI_NOALLOC_MAX_EXPERTS (larger sizes return
+ * CTI_ERR_UNSUPPORTED).  All calls on a device share the array, so calls
+ * that overlap on the GPU race; serialise them.  The first call on each
+ * device resolves the array's address and should come before any stream
+ * capture.
+ * ---------------------------------------------------------------------- */
+#define CTI_NOALLOC_MAX_TOKENS 131072
+#define CTI_NOALLOC_MAX_EXPERTS 128
+int cti_moe_route_dispatch_noalloc(const void* x_bf16, const float* wg, const float* bg,
+                                   int64_t T, int D, int E, int renorm, int32_t* idx2,
+                                   float* gate2, int32_t* offsets, int32_t* perm_inv,
+                                   int32_t* sorted_token, void* xperm_bf16, int32_t* status,
+                                   void* stream);
+
+/* ------------------------------------------------------------------------
  * Stage 3 - grouped expert GEMM on tcgen05 tensor cores.
  * Replaces moe_sparse_fc1*_kernel and moe_sparse_fc2*_kernel
  * (online_best/infer.py:1293-1600) and Expert.forward (baseline/infer.py:
