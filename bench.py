@@ -181,7 +181,7 @@ def cpu_baseline_moe(cfg, seconds: float, sample_tokens: int = CPU_SAMPLE_TOKENS
                 break
     return {"value": n * S / el, "unit": "tokens/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{S} of the {T} configuration-2 tokens per call, {n} calls "
+            "sample": f"{S} of the {T} {cfg.name} tokens per call, {n} calls "
                       f"({el:.1f} s), fp32, oracle/moe_ref.py (baseline/infer.py:280-358)"}
 
 
@@ -400,6 +400,144 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_ep(args, world, rank, local):
+    """--config cfg5: the expert-parallel layer (d_model 1024, 64 experts,
+    d_ff 4096) over T = 262,144 tokens in total, split evenly across the N
+    ranks; rank r owns experts [r*64/N, (r+1)*64/N).  Total work is fixed as
+    N grows (strong scaling); N = 1 is the single-GPU baseline (no
+    exchange)."""
+    from cti_b200 import _lib, synth
+    from cti_b200.ep import ExpertParallelSMoE
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = synth.CFG5
+    T = cfg.tokens
+    D, E, F = cfg.d_model, cfg.num_experts, cfg.dim_ff
+    w = synth.moe_weights(D, E, F, cfg.zipf_bias, seed=0, device=dev)
+    m = ExpertParallelSMoE(D, F, E).to(dev)
+    m.load_weights(w.wg, w.bg, w.w1, w.b1, w.w2, w.b2)
+    m.prepare_for_inference()
+    del w
+    lo, hi = rank * T // world, (rank + 1) * T // world
+    x = synth.moe_activations(T, D, seed=0, device=dev)[lo:hi].clone()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    torch.cuda.empty_cache()
+
+    for _ in range(args.warmup):
+        m(x)
+    torch.cuda.synchronize(dev)
+    _lib.raise_on_status(dev)
+
+    sampler = ClockSampler(dev) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.start()
+    times = time_steps(lambda: m(x), args.steps, flush, dev)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    _lib.raise_on_status(dev)
+    step_ms = max_over_ranks(statistics.mean(times), world, dev)
+    value = T / (step_ms / 1e3)
+
+    # End to end: this rank's tokens from pinned host memory, output back.
+    x_h = x.cpu().pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+    x_d = torch.empty_like(x)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        out, _ = m(x_d)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e2e_times = time_steps(e2e_step, args.steps, flush, dev, hide_host=False)
+    barrier(world)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+
+    # Stage split (CUDA events between the stages of one forward), median of
+    # a few forwards, per rank; rows = rows this rank's experts computed.
+    names = ["router", "dispatch", "exchange", "experts", "exchange_back", "combine"]
+    per = {n: [] for n in names}
+    rows_local = 0
+    for _ in range(5):
+        flush.zero_()
+        evs = [torch.cuda.Event(enable_timing=True)]
+        evs[0].record()
+
+        def mark(name, evs=evs):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append(e)
+
+        m(x, mark=mark)
+        torch.cuda.synchronize(dev)
+        for n, a, b in zip(names, evs[:-1], evs[1:]):
+            per[n].append(a.elapsed_time(b))
+    stages = {n: statistics.median(v) for n, v in per.items()}
+    from cti_b200 import ops
+    r = ops.router(x, m._wg, m._bg)
+    cnt = torch.bincount(r.idx2.reshape(-1).long(), minlength=E).to(torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(cnt)
+    El = E // world
+    rows_per_rank = cnt.view(world, El).sum(dim=1).tolist()
+    rows_local = rows_per_rank[rank]
+    exp_ms = torch.tensor([stages["experts"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        gathered = [torch.empty_like(exp_ms) for _ in range(world)]
+        dist.all_gather(gathered, exp_ms)
+        experts_ms = [float(t.item()) for t in gathered]
+    else:
+        experts_ms = [stages["experts"]]
+    flops_local = 4.0 * rows_local * D * F
+    achieved = flops_local / (stages["experts"] / 1e3) / 1e12
+    peaks, peak_src = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    total_flops = 4.0 * 2 * T * D * F
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_moe(cfg, args.cpu_seconds, sample_tokens=1024)
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"cfg5: expert-parallel Top-2 MoE layer, d_model {D}, {E} experts, "
+                               f"d_ff {F}, {T} tokens in total split evenly over the ranks",
+                   "tokens": T, "d_model": D, "experts": E, "d_ff": F,
+                   "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single "
+                   "(counts, then rows with uneven splits; the same back)" if world > 1
+                   else "none (one rank)",
+                   "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": x_h.numel() * x_h.element_size() * world,
+                "d2h_bytes_per_step": out_h.numel() * out_h.element_size() * world},
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (fc1 + fc2, rank 0)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": f"bf16_tflops of {peak_src}",
+                     "flops_per_launch": flops_local / 2, "traffic": None},
+        "layer_roofline_frac": total_flops / (step_ms / 1e3) / 1e12 / world / peak,
+        "stages_ms_rank0": stages,
+        "rows_per_rank": rows_per_rank,
+        "experts_ms_per_rank": experts_ms,
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_profile_workload(args):
     """--profile STAGE: the configuration-2 workload with one stage launched
     warmup + steps times and nothing else timed; the small, self-contained
@@ -517,8 +655,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3"],
-                    help="cfg2: MoE layer (default, the headline); cfg3: embedding bag")
+    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg5"],
+                    help="cfg2: MoE layer (default, the headline); cfg3: embedding bag; "
+                         "cfg5: expert-parallel MoE layer (strong scaling over N)")
     ap.add_argument("--profile", default=None,
                     choices=["router", "dispatch", "ffn_fused", "ffn_fc1", "combine", "layer",
                              "embbag"],
@@ -537,6 +676,8 @@ def main():
     try:
         if args.config == "cfg3":
             run_embbag(args, world, rank, local)
+        elif args.config == "cfg5":
+            run_ep(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
