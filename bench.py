@@ -44,6 +44,7 @@ import torch  # noqa: E402
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
 CPU_SAMPLE_TOKENS = 8192
+CALIBRATION_TOKENS = 65536
 
 
 def load_peaks():
@@ -407,7 +408,7 @@ def run_ep(args, world, rank, local):
     N grows (strong scaling); N = 1 is the single-GPU baseline (no
     exchange)."""
     from cti_b200 import _lib, synth
-    from cti_b200.ep import ExpertParallelSMoE
+    from cti_b200.ep import ExpertParallelSMoE, balanced_placement
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -415,7 +416,21 @@ def run_ep(args, world, rank, local):
     T = cfg.tokens
     D, E, F = cfg.d_model, cfg.num_experts, cfg.dim_ff
     w = synth.moe_weights(D, E, F, cfg.zipf_bias, seed=0, device=dev)
-    m = ExpertParallelSMoE(D, F, E).to(dev)
+    placement = None
+    if args.placement == "balanced" and world > 1:
+        # Calibrate on a separate batch (seed 1): its routing counts,
+        # summed over the ranks, give each expert's expected load.
+        from cti_b200 import ops
+
+        xc = synth.moe_activations(CALIBRATION_TOKENS, D, seed=1, device=dev)
+        rc = ops.router(xc, w.wg.float().contiguous(), w.bg.float().contiguous())
+        load = torch.bincount(rc.idx2.reshape(-1).long(), minlength=E).to(torch.float64)
+        import torch.distributed as dist
+
+        dist.all_reduce(load)
+        placement = balanced_placement(load.tolist(), world)
+        del xc, rc
+    m = ExpertParallelSMoE(D, F, E, placement=placement).to(dev)
     m.load_weights(w.wg, w.bg, w.w1, w.b1, w.w2, w.b2)
     m.prepare_for_inference()
     del w
@@ -434,7 +449,8 @@ def run_ep(args, world, rank, local):
     torch.cuda.synchronize(dev)
     if sampler:
         sampler.start()
-    times = time_steps(lambda: m(x), args.steps, flush, dev)
+    overlap = args.ep_exchange == "p2p"
+    times = time_steps(lambda: m(x, overlap=overlap), args.steps, flush, dev)
     torch.cuda.synchronize(dev)
     barrier(world)
     clocks = sampler.stop() if sampler else None
@@ -449,7 +465,7 @@ def run_ep(args, world, rank, local):
 
     def e2e_step():
         x_d.copy_(x_h, non_blocking=True)
-        out, _ = m(x_d)
+        out, _ = m(x_d, overlap=overlap)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
@@ -475,7 +491,7 @@ def run_ep(args, world, rank, local):
             e.record()
             evs.append(e)
 
-        m(x, mark=mark)
+        m(x, mark=mark, overlap=overlap)
         torch.cuda.synchronize(dev)
         for n, a, b in zip(names, evs[:-1], evs[1:]):
             per[n].append(a.elapsed_time(b))
@@ -488,7 +504,7 @@ def run_ep(args, world, rank, local):
 
         dist.all_reduce(cnt)
     El = E // world
-    rows_per_rank = cnt.view(world, El).sum(dim=1).tolist()
+    rows_per_rank = cnt.view(world, El).sum(dim=1).tolist()  # router outputs are slots
     rows_local = rows_per_rank[rank]
     exp_ms = torch.tensor([stages["experts"]], dtype=torch.float64, device=dev)
     if world > 1:
@@ -515,9 +531,16 @@ def run_ep(args, world, rank, local):
         "config": {"workload": f"cfg5: expert-parallel Top-2 MoE layer, d_model {D}, {E} experts, "
                                f"d_ff {F}, {T} tokens in total split evenly over the ranks",
                    "tokens": T, "d_model": D, "experts": E, "d_ff": F,
-                   "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single "
-                   "(counts, then rows with uneven splits; the same back)" if world > 1
-                   else "none (one rank)",
+                   "parallelism": f"ep{world}",
+                   "placement": "contiguous" if placement is None else
+                   f"balanced (LPT over the routing counts of a separate {CALIBRATION_TOKENS}-token "
+                   "calibration batch)",
+                   "exchange": ("none (one rank)" if world == 1 else
+                                "counts: NCCL all_to_all_single; rows: NCCL point-to-point per "
+                                "peer, overlapped with the experts over the rows a rank routes to "
+                                "itself; results back the same way" if overlap else
+                                "NCCL all_to_all_single (counts, then rows with uneven splits; "
+                                "the same back)"),
                    "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
                    "l2": "flushed (256 MiB write) before every timed step"},
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
@@ -658,6 +681,10 @@ def main():
     ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg5"],
                     help="cfg2: MoE layer (default, the headline); cfg3: embedding bag; "
                          "cfg5: expert-parallel MoE layer (strong scaling over N)")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="cfg5 expert placement over the ranks")
+    ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "all_to_all"],
+                    help="cfg5 rows exchange: overlapped point-to-point or plain all_to_all")
     ap.add_argument("--profile", default=None,
                     choices=["router", "dispatch", "ffn_fused", "ffn_fc1", "combine", "layer",
                              "embbag"],

@@ -101,3 +101,105 @@ def test_send_counts_follow_contiguous_expert_blocks():
     assert ep.rank_send_counts(counts, 4) == [3, 6, 4, 7]
     offs = ep.received_group_offsets(torch.tensor([[1, 2], [0, 4]]))
     assert offs.tolist() == [0, 1, 3, 3, 7]
+
+
+def test_balanced_placement_evens_out_zipf_load():
+    sys.path.insert(0, str(ROOT))
+    import cti_b200.ep as ep
+    from cti_b200 import synth
+
+    E = 64
+    p = torch.softmax(synth.zipf_router_bias(E, 1.2, seed=0), 0)
+    for world in (2, 4, 8):
+        place = ep.balanced_placement(p.tolist(), world)
+        assert sorted(place) == list(range(E))
+        per = E // world
+        for r in range(world):
+            assert place[r * per:(r + 1) * per] == sorted(place[r * per:(r + 1) * per])
+        loads = [float(p[place[r * per:(r + 1) * per]].sum()) for r in range(world)]
+        contiguous = [float(p[r * per:(r + 1) * per].sum()) for r in range(world)]
+        assert max(loads) <= max(contiguous) + 1e-12
+        # LPT bound: max load <= mean + the largest single expert.
+        assert max(loads) <= 1.0 / world + float(p.max()) + 1e-12
+    with pytest.raises(ValueError):
+        ep.balanced_placement([1.0] * 6, 4)
+
+
+def _layer_worker(rank, world, port, splits, overlap, balanced):
+    """ExpertParallelSMoE.forward itself on gloo ranks: its compute stages
+    (router, dispatch, expert FFN, combine - CUDA kernels in the product)
+    are replaced by the CPU oracle, everything else is the product code."""
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        import types
+
+        import cti_b200.ep as ep
+        from cti_b200 import ops as real_ops
+        from oracle import moe_ref as mr
+
+        torch.set_num_threads(1)
+        D, E, F = 32, 8, 64
+        T = sum(splits)
+        x, wg, bg, w1, b1, w2, b2 = _problem(D, E, F, T, 11)
+
+        def router(x2, wg_, bg_, renorm=True):
+            g = mr.gate_ref(x2, wg_, bg_, renorm=renorm, tie_lower_id=True)
+            return real_ops.RouterOut(g.idx.int(), g.score.float(), None, None)
+
+        def dispatch(x2, r, n):
+            offsets, sorted_token, perm_inv = mr.expert_segments(r.idx2.long(), n)
+            return real_ops.DispatchOut(offsets.int(), perm_inv.int(), sorted_token.int(),
+                                        x2[sorted_token.long()])
+
+        def combine(y, perm_inv, gate2):
+            pi = perm_inv.long()
+            return gate2[:, :1] * y[pi[:, 0]] + gate2[:, 1:] * y[pi[:, 1]]
+
+        fake = types.SimpleNamespace(router=router, dispatch=dispatch, combine=combine)
+        orig_ops, orig_prep = ep.ops, ep._prepare_x
+        ep.ops, ep._prepare_x = fake, lambda t: t.contiguous()
+        try:
+            placement = None
+            if balanced:
+                placement = ep.balanced_placement(torch.softmax(bg, 0).tolist(), world)
+            m = ep.ExpertParallelSMoE(D, F, E, placement=placement)
+            m.load_weights(wg, bg, w1, b1, w2, b2)
+            m.prepare_for_inference()
+
+            def ffn_rows(rows, offs, first=0):
+                y = torch.empty_like(rows)
+                o = offs.long().tolist()
+                for grp in range(len(o) - 1):
+                    if o[grp + 1] > o[grp]:
+                        ex = m.experts[first + grp % (m.local_experts - first)]
+                        y[o[grp]:o[grp + 1]] = mr.expert_ref(
+                            rows[o[grp]:o[grp + 1]], ex.fc1.weight, ex.fc1.bias,
+                            ex.fc2.weight, ex.fc2.bias, "gelu")
+                return y
+
+            m._expert_ffn = ffn_rows
+            m._ffn_into = lambda rows, offs, out, first_expert=0: out.copy_(
+                ffn_rows(rows, offs, first_expert))
+            lo = sum(splits[:rank])
+            marks = []
+            out, aux = m(x[lo:lo + splits[rank]], mark=marks.append, overlap=overlap)
+        finally:
+            ep.ops, ep._prepare_x = orig_ops, orig_prep
+        assert aux is None
+        assert marks == ["router", "dispatch", "exchange", "experts", "exchange_back", "combine"]
+        ref, _ = mr.smoe_ref(x, wg, bg, w1, b1, w2, b2, act="gelu", renorm=True)
+        torch.testing.assert_close(out, ref[lo:lo + splits[rank]], rtol=1e-5, atol=1e-6)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("splits,overlap,balanced", [
+    ([40, 56], True, False), ([40, 56], False, True), ([0, 37], True, True),
+    ([25, 0, 31, 12], True, True), ([25, 9, 31, 12], False, False)])
+def test_expert_parallel_layer_forward_on_gloo(splits, overlap, balanced):
+    world = len(splits)
+    mp.spawn(_layer_worker, args=(world, _free_port(), splits, overlap, balanced), nprocs=world,
+             join=True)

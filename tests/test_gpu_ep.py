@@ -24,7 +24,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, D, E, F, T):
+def _worker(rank, world, port, D, E, F, T, balanced, overlap):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -48,9 +48,15 @@ def _worker(rank, world, port, D, E, F, T):
         synth.load_moe_module(full, w)
         x = synth.moe_activations(T, D, seed=5)
         lo, hi = rank * T // world, (rank + 1) * T // world
-        ep = ExpertParallelSMoE(D, F, E).to(dev)
+        placement = None
+        if balanced:
+            from cti_b200.ep import balanced_placement
+            placement = balanced_placement(torch.softmax(w.bg, 0).tolist(), world)
+            if world > 1:
+                assert placement != list(range(E))
+        ep = ExpertParallelSMoE(D, F, E, placement=placement).to(dev)
         ep.load_global_state_dict(full.state_dict())
-        out, _ = ep(x[lo:hi].to(dev))
+        out, _ = ep(x[lo:hi].to(dev), overlap=overlap)
         _lib.raise_on_status(dev)
         full.to(dev).prepare_for_inference()
         ref_gpu, _ = full(x[lo:hi].to(dev).unsqueeze(0))
@@ -63,8 +69,12 @@ def _worker(rank, world, port, D, E, F, T):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("D,E,F,T", [(1024, 64, 4096, 8192), (256, 16, 1024, 6000)])
-def test_expert_parallel_layer_matches_single_gpu(D, E, F, T):
+@pytest.mark.parametrize("D,E,F,T,balanced,overlap", [(1024, 64, 4096, 8192, False, False),
+                                                      (1024, 64, 4096, 8192, True, True),
+                                                      (256, 16, 1024, 6000, True, True),
+                                                      (256, 16, 1024, 6000, False, True)])
+def test_expert_parallel_layer_matches_single_gpu(D, E, F, T, balanced, overlap):
     world = min(2, torch.cuda.device_count())
     assert world >= 1
-    mp.spawn(_worker, args=(world, _free_port(), D, E, F, T), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), D, E, F, T, balanced, overlap), nprocs=world,
+             join=True)
