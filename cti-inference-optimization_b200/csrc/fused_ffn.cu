@@ -10,27 +10,33 @@
 //
 // Per tile (128 token rows of one expert), d_ff is processed in 128-wide
 // chunks c:
-//   GEMM1(c): acc1[c%2] (TMEM, 128 cols) = X[128, D] @ W1[e][c*128:+128, :]^T
-//   epilogue: acc1 -> +b1 -> GELU -> bf16 -> H (shared memory, laid out
-//             exactly as a TMA 128-byte-swizzled K-major tile)
-//   GEMM2(c): acc2 (TMEM, D cols) += H @ W2[e][:, c*128:+128]^T
-// The MMA thread issues GEMM2(c) only after GEMM1(c+2), so the tensor core
-// works on other chunks while the epilogue warps run the GELU of chunk c.
+//   GEMM1(c): acc1[c%2] (TMEM, 128 fp32 cols) = X[128, D] @ W1[e][c*128:+128, :]^T
+//   epilogue: acc1 -> +b1 -> GELU -> bf16 -> H(c), written back into the
+//             same TMEM columns (two bf16 per 32-bit column)
+//   GEMM2(c): acc2 (TMEM, D cols) += H(c) @ W2[e][:, c*128:+128]^T, with the
+//             A operand read from tensor memory
+// The MMA thread issues GEMM2(c) right after GEMM1(c+1), and GEMM1(c+2) - which
+// overwrites acc1[c%2] - after GEMM2(c): tcgen05.mma instructions of one thread
+// execute in issue order, so GEMM2(c) has read H(c) before GEMM1(c+2) writes
+// there, and the hidden tile never touches shared memory.  While the epilogue
+// turns chunk c into H(c), the tensor core runs GEMM2(c-1) and GEMM1(c+1).
 // After the last chunk, acc2 + b2 is written to Y as bf16.
 //
-// Roles (576 threads): warp 0 TMA producer (X tile once per tile; W1/W2
-// slabs through a ring of 32 KB stages), warp 1 TMEM owner and MMA issuer
+// Roles (576 threads): warp 0 TMA producer (X tile once per tile; W1 and W2
+// chunks through two rings of whole-chunk slots), warp 1 TMEM owner and MMA issuer
 // (tcgen05.mma M=128, K=16, bf16 -> fp32; N=128 for GEMM1, N=D for GEMM2),
-// warps 2-17 epilogue
-// (four warps per TMEM lane quadrant, each owning 32 of a chunk's 128
-// columns and a quarter of the output columns; the expert's biases are
-// staged in shared memory once per expert change).
+// warps 2-17 epilogue (four warps per TMEM lane quadrant, each owning 32 of
+// a chunk's 128 columns and a quarter of the output columns; the expert's
+// biases are staged in shared memory once per expert change).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
-// Shared memory (D=256): X 64 KB + H 32 KB + ring 3x32 KB + biases 5 KB +
-// scheduler 2 KB.  One H buffer suffices with the two-chunk lag: the
-// epilogue writes H(c) after GEMM2(c-1) has read H(c-1), still well before
-// GEMM2(c) is due.  d_ff <= 1024 (one expert's b1 in shared memory).
+// The epilogue thread that owns fp32 columns [32s, 32s+32) of acc1 writes its
+// 32 bf16 hidden values to columns [32s, 32s+16) of the same buffer, so each
+// 16-wide K step of GEMM2 reads 8 contiguous columns at 32*(k/2) + 8*(k%2).
+// Shared memory: X tile (D/64 slabs of 16 KB) + one W1 and one W2 slot of
+// 64 KB each for D=256 (two of 32 KB each for D=128) + biases 5 KB +
+// scheduler 2 KB.
+// d_ff <= 1024 (one expert's b1 in shared memory).
 #include "common.cuh"
 #include "gelu.cuh"
 #include "sched.cuh"
@@ -43,49 +49,40 @@ constexpr int kBM = 128;
 constexpr int kFC = 128;           // d_ff chunk
 constexpr int kBK = 64;            // bf16 elements per 128-byte swizzled row
 constexpr int kSlab = kBM * kBK * 2;  // 16 KB: one 128x64 bf16 tile
-// Weight ring stages of 32 KB: each wait on a stage covers 8 MMAs (GEMM1,
-// N=128) or 4 MMAs of N=256 (GEMM2), enough tensor work to hide the cost of
-// the wait and fence on the issuing thread.
-constexpr int kStage = 2 * kSlab;
 constexpr int kEpiWarps = 16;
 constexpr int kMaxF = 1024;  // b1 of one expert staged in shared memory
 using Sched = GroupSchedT<256>;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr uint32_t kAcc1Col = 256;
-// GEMM2 of chunk c is issued after GEMM1 of chunk c+kLag: between the end of
-// GEMM1(c) and the start of GEMM2(c) the tensor core has 2*kLag GEMMs of other
-// chunks to run, which is the time the epilogue has for the GELU of chunk c.
-constexpr int kLag = 2;
+// GEMM2 of chunk c is issued after GEMM1 of chunk c+kLag.  H(c) lives in
+// acc1[c%2], so kLag must be 1: GEMM1(c+2) reuses that buffer.
+constexpr int kLag = 1;
 
+// Weights stream through two rings of slots, one for W1 chunks ([128 x D])
+// and one for W2 chunks ([D x 128]).  A slot holds one whole chunk and has
+// ONE full barrier, so the MMA thread tests a barrier once per GEMM: on
+// sm_100 every mbarrier test on the MMA-issuing thread costs ~200 cycles of
+// MMA issue, more than the slack of a burst of N=128 MMAs (~14 cycles each
+// above the ~50-cycle issue interval), while commits are cheap (~12).  Each
+// slot has two empty barriers, one per half (the MMA commits after each
+// half), so the producer refills the first half while the tensor core still
+// reads the second.
 template <int D>
 struct FF {
   static constexpr int XK = D / kBK;          // X k-slabs
-  static constexpr int G1S = XK / 2;          // ring stages of W1 per chunk (2 k-slabs each)
-  static constexpr int KPS2 = kStage / (D * kBK * 2);  // W2 k-slabs [D x 64] per stage
-  static constexpr int G2S = 2 / KPS2;        // ring stages of W2 per chunk
-  static constexpr int STAGES = D == 256 ? 3 : 4;
+  static constexpr int W1H = XK / 2;          // W1 k-slabs [128 x 64] per half slot
+  static constexpr size_t W1C = (size_t)kFC * D * 2;  // bytes of one W1 chunk
+  static constexpr size_t W2H = (size_t)D * kBK * 2;  // one W2 k-slab [D x 64] = half a chunk
+  static constexpr size_t W2C = 2 * W2H;
+  static constexpr int NSLOT = D == 256 ? 1 : 2;      // slots per ring
   static constexpr size_t X_BYTES = (size_t)XK * kSlab;
-  static constexpr size_t H_BYTES = (size_t)2 * kSlab;  // one 128x128 hidden chunk
-  static constexpr size_t RING_BYTES = (size_t)STAGES * kStage;
+  static constexpr size_t RING_BYTES = (size_t)NSLOT * (W1C + W2C);
   static constexpr size_t BIAS_BYTES = (size_t)(kMaxF + D) * 4;
   static constexpr size_t SMEM =
-      1024 + X_BYTES + H_BYTES + RING_BYTES + BIAS_BYTES + Sched::smem_bytes() + 256;
+      1024 + X_BYTES + RING_BYTES + BIAS_BYTES + Sched::smem_bytes() + 256;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
-
-// Writes 32 consecutive bf16 columns (four 16-byte chunks, starting at
-// chunk j0 of the row) of row r into a 128x64 K-major slab with the
-// 128-byte swizzle (chunk j of row r lives at chunk position j ^ (r % 8)),
-// the layout TMA produces and UMMA reads.
-CTI_DEVICE void store_row32_swizzled(uint8_t* slab, int r, int j0, const uint32_t (&w)[16]) {
-  uint8_t* row = slab + r * 128;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int pos = (j0 + j) ^ (r & 7);
-    *reinterpret_cast<uint4*>(row + pos * 16) =
-        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-  }
-}
 
 // One arrival per warp: the lanes' prior writes are ordered before lane 0's
 // (release) arrive by the warp barrier.  Barriers signalled this way count
@@ -108,21 +105,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sx = smem;
-  uint8_t* sh = sx + P::X_BYTES;
-  uint8_t* ring = sh + P::H_BYTES;
+  uint8_t* ring = sx + P::X_BYTES;
+  uint8_t* ring1 = ring;                          // W1 slots
+  uint8_t* ring2 = ring + P::NSLOT * P::W1C;      // W2 slots
   float* b1s = reinterpret_cast<float*>(ring + P::RING_BYTES);
   float* b2s = b1s + kMaxF;
   uint8_t* sched_mem = reinterpret_cast<uint8_t*>(b2s + D);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + Sched::smem_bytes());
-  uint64_t* full = bars;
-  uint64_t* empty = full + P::STAGES;
-  uint64_t* x_full = empty + P::STAGES;
+  uint64_t* full1 = bars;                // [NSLOT] W1 chunk landed
+  uint64_t* empty1 = full1 + P::NSLOT;   // [NSLOT][2] W1 half read by the MMAs
+  uint64_t* full2 = empty1 + 2 * P::NSLOT;
+  uint64_t* empty2 = full2 + P::NSLOT;
+  uint64_t* x_full = empty2 + 2 * P::NSLOT;
   uint64_t* x_empty = x_full + 1;
-  uint64_t* a1_full = x_empty + 1;  // [2]
-  uint64_t* a1_empty = a1_full + 2;  // [2]
-  uint64_t* h_full = a1_empty + 2;
-  uint64_t* h_empty = h_full + 1;
-  uint64_t* a2_full = h_empty + 1;
+  uint64_t* a1_full = x_empty + 1;  // [2] GEMM1(c) done -> epilogue
+  uint64_t* h_full = a1_full + 2;    // [2] H(c) written -> MMA
+  uint64_t* a2_full = h_full + 2;
   uint64_t* a2_empty = a2_full + 1;
   uint64_t* drain = a2_empty + 1;
   uint64_t* bfree = drain + 1;   // epilogue threads done with the staged biases
@@ -135,18 +133,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nch = F / kFC;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P::STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < P::NSLOT; ++s) {
+      mbar_init(&full1[s], 1);
+      mbar_init(&full2[s], 1);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(&empty1[2 * s + h], 1);
+        mbar_init(&empty2[2 * s + h], 1);
+      }
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a1_full[i], 1);
-      mbar_init(&a1_empty[i], kEpiWarps);
+      mbar_init(&h_full[i], kEpiWarps);
     }
-    mbar_init(h_full, kEpiWarps);
-    mbar_init(h_empty, 1);
     mbar_init(a2_full, 1);
     mbar_init(a2_empty, kEpiWarps);
     mbar_init(drain, 1);
@@ -175,23 +175,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int64_t issued = 0, x_issued = 0;
+      int64_t n1 = 0, n2 = 0, x_issued = 0;  // chunks loaded into each ring
       int it = 0;
       bool ok = true;
-      // Claims the next ring stage (bounded wait) and arms it for kStage bytes.
-      auto acquire = [&]() -> uint8_t* {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, status, 0x201, abort_flag)) return nullptr;
-        mbar_arrive_expect_tx(&full[stage], kStage);
-        return ring + stage * kStage;
-      };
-      auto advance = [&]() {
-        ++issued;
-        if (++stage == P::STAGES) {
-          stage = 0;
-          phase ^= 1u;
+      // Loads one chunk into the next slot of a ring: per half, wait until
+      // the MMAs have read that half of the slot's previous chunk; the full
+      // barrier is armed once, for the whole chunk, before the first load.
+      auto load_chunk = [&](uint8_t* ring_base, size_t chunk_bytes, uint64_t* full,
+                            uint64_t* empty, int64_t& n, int where, auto&& issue_half) -> bool {
+        const int slot = (int)(n % P::NSLOT);
+        const uint32_t ph = (uint32_t)((n / P::NSLOT) & 1);
+        uint8_t* buf = ring_base + (size_t)slot * chunk_bytes;
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&empty[2 * slot + h], ph ^ 1u, status, where, abort_flag)) return false;
+          if (h == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)chunk_bytes);
+          issue_half(buf, &full[slot], h);
+          // Counted once its first loads are in flight, so that the drain
+          // below waits for them even if the second half is never issued.
+          if (h == 0) ++n;
         }
+        return true;
       };
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         const TileCoord tc = sched.decode(t);
@@ -202,41 +205,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
         ++x_issued;
         for (int s = 0; s < nch + kLag && ok; ++s) {
-          if (s < nch) {  // W1 rows [s*128, +128), two 64-wide k-slabs per stage
-            for (int j = 0; j < P::G1S && ok; ++j) {
-              uint8_t* buf = acquire();
-              if (!buf) {
-                ok = false;
-                break;
-              }
-              for (int h = 0; h < 2; ++h)
-                tma_load_2d(buf + h * kSlab, &tmW1, &full[stage], (2 * j + h) * kBK,
-                            gw * F + s * kFC);
-              advance();
-            }
+          if (s < nch) {  // W1 rows [s*128, +128): k-slabs [128 x 64], W1H per half
+            ok = load_chunk(ring1, P::W1C, full1, empty1, n1, 0x201,
+                            [&](uint8_t* buf, uint64_t* bar, int h) {
+                              for (int j = 0; j < P::W1H; ++j) {
+                                const int kb = h * P::W1H + j;
+                                tma_load_2d(buf + kb * kSlab, &tmW1, bar, kb * kBK,
+                                            gw * F + s * kFC);
+                              }
+                            });
           }
-          if (s >= kLag && ok) {  // W2 [D rows, 64 k] slabs of chunk s-kLag
+          if (s >= kLag && ok) {  // W2 [D rows, 64 k] k-slab h of chunk s-kLag
             const int c = s - kLag;
-            for (int j = 0; j < P::G2S && ok; ++j) {
-              uint8_t* buf = acquire();
-              if (!buf) {
-                ok = false;
-                break;
-              }
-              for (int h = 0; h < P::KPS2; ++h)
-                tma_load_2d(buf + h * (D * kBK * 2), &tmW2, &full[stage],
-                            c * kFC + (j * P::KPS2 + h) * kBK, gw * D);
-              advance();
-            }
+            ok = load_chunk(ring2, P::W2C, full2, empty2, n2, 0x203,
+                            [&](uint8_t* buf, uint64_t* bar, int h) {
+                              tma_load_2d(buf + h * P::W2H, &tmW2, bar, c * kFC + h * kBK,
+                                          gw * D);
+                            });
           }
         }
       }
       // Let every load this thread issued land before the CTA can exit.
-      for (int i = 1; i <= P::STAGES && i <= issued; ++i) {
-        const int64_t n = issued - i;
-        mbar_wait(&full[n % P::STAGES], (uint32_t)((n / P::STAGES) & 1), status, 0x203, nullptr);
+      for (int i = 1; i <= P::NSLOT; ++i) {
+        if (n1 - i >= 0)
+          mbar_wait(&full1[(n1 - i) % P::NSLOT], (uint32_t)(((n1 - i) / P::NSLOT) & 1), status,
+                    0x204, nullptr);
+        if (n2 - i >= 0)
+          mbar_wait(&full2[(n2 - i) % P::NSLOT], (uint32_t)(((n2 - i) / P::NSLOT) & 1), status,
+                    0x204, nullptr);
       }
-      (void)kSlab;
       if (x_issued > 0) mbar_wait(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x204, nullptr);
     }
   } else if (warp == 1) {
@@ -244,94 +241,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc1 = idesc_bf16_f32(kBM, 128);  // GEMM1: N = d_ff chunk
       const uint32_t idesc2 = idesc_bf16_f32(kBM, D);    // GEMM2: N = d_model
-      int stage = 0;
-      uint32_t phase = 0;
+      int64_t n1 = 0, n2 = 0;  // chunks consumed from each weight ring
       int it = 0;
       bool any = false, ok = true;
       const uint32_t x_addr = smem_u32(sx);
-      const uint32_t h_addr = smem_u32(sh);
-      const uint32_t ring_addr = smem_u32(ring);
-      auto advance = [&]() {
-        if (++stage == P::STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      };
+      const uint32_t ring1_addr = smem_u32(ring1);
+      const uint32_t ring2_addr = smem_u32(ring2);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         if (!mbar_wait(x_full, (uint32_t)(it & 1), status, 0x205, abort_flag)) break;
         tc_fence_after();
         for (int s = 0; s < nch + kLag && ok; ++s) {
           if (s < nch) {  // GEMM1(s)
+            // acc1[b] last held H(s-2), read by GEMM2(s-2), which this
+            // thread issued before: no wait needed.
             const int64_t gc = (int64_t)it * nch + s;
             const int b = (int)(gc & 1);
-            const uint32_t k = (uint32_t)(gc >> 1);
-            if (!mbar_wait(&a1_empty[b], (k & 1u) ^ 1u, status, 0x206, abort_flag)) {
+            const uint32_t d = tmem_base + kAcc1Col + (uint32_t)b * 128u;
+            const int slot = (int)(n1 % P::NSLOT);
+            if (!mbar_wait(&full1[slot], (uint32_t)((n1 / P::NSLOT) & 1), status, 0x207,
+                           abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t d = tmem_base + kAcc1Col + (uint32_t)b * 128u;
-            for (int j = 0; j < P::G1S; ++j) {
-              if (!mbar_wait(&full[stage], phase, status, 0x207, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t b0 = ring_addr + stage * kStage;
+            const uint32_t b0 = ring1_addr + (uint32_t)(slot * P::W1C);
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int kb = 2 * j + h;
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+              for (int j = 0; j < P::W1H; ++j) {
+                const int kb = h * P::W1H + j;
                 const uint32_t a0 = x_addr + kb * kSlab;
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
                   umma_bf16(d, smem_desc_sw128(a0 + kk * 32),
-                            smem_desc_sw128(b0 + h * kSlab + kk * 32), idesc1,
+                            smem_desc_sw128(b0 + kb * kSlab + kk * 32), idesc1,
                             (kb | kk) != 0 ? 1u : 0u);
               }
-              any = true;
-              umma_commit(&empty[stage]);
-              advance();
+              umma_commit(&empty1[2 * slot + h]);
             }
-            if (!ok) break;
+            any = true;
+            ++n1;
             umma_commit(&a1_full[b]);
             if (s == nch - 1) umma_commit(x_empty);
           }
-          if (s >= kLag) {  // GEMM2(s-kLag), N = D in one instruction
+          if (s >= kLag) {  // GEMM2(s-kLag), N = D in one instruction, A = H in TMEM
             const int c = s - kLag;
             const int64_t gc = (int64_t)it * nch + c;
+            const int b = (int)(gc & 1);
+            const uint32_t k = (uint32_t)(gc >> 1);
             if (c == 0) {
               if (!mbar_wait(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x208, abort_flag)) {
                 ok = false;
                 break;
               }
             }
-            if (!mbar_wait(h_full, (uint32_t)(gc & 1), status, 0x209, abort_flag)) {
+            if (!mbar_wait(&h_full[b], k & 1u, status, 0x209, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const int slot = (int)(n2 % P::NSLOT);
+            if (!mbar_wait(&full2[slot], (uint32_t)((n2 / P::NSLOT) & 1), status, 0x20a,
+                           abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            for (int j = 0; j < P::G2S; ++j) {
-              if (!mbar_wait(&full[stage], phase, status, 0x20a, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t b0 = ring_addr + stage * kStage;
+            const uint32_t h_tmem = tmem_base + kAcc1Col + (uint32_t)b * 128u;
+            const uint32_t b0 = ring2_addr + (uint32_t)(slot * P::W2C);
 #pragma unroll
-              for (int h = 0; h < P::KPS2; ++h) {
-                const int kb = j * P::KPS2 + h;
-                const uint32_t a0 = h_addr + kb * kSlab;
+            for (int h = 0; h < 2; ++h) {  // k-slab h: K columns [64h, 64h+64) of the chunk
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk)
-                  umma_bf16(tmem_base, smem_desc_sw128(a0 + kk * 32),
-                            smem_desc_sw128(b0 + h * (D * kBK * 2) + kk * 32), idesc2,
-                            (c | kb | kk) != 0 ? 1u : 0u);
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                const int k16 = h * (kBK / 16) + kk;  // 16-wide K step within the chunk
+                umma_bf16_ts(tmem_base, h_tmem + (uint32_t)((k16 >> 1) * 32 + (k16 & 1) * 8),
+                             smem_desc_sw128(b0 + (uint32_t)(h * P::W2H) + kk * 32), idesc2,
+                             (c | h | kk) != 0 ? 1u : 0u);
               }
-              umma_commit(&empty[stage]);
-              advance();
+              umma_commit(&empty2[2 * slot + h]);
             }
-            if (!ok) break;
-            umma_commit(h_empty);
+            ++n2;
             if (c == nch - 1) umma_commit(a2_full);
           }
         }
@@ -379,32 +367,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col +
+                               (uint32_t)b * 128u + (uint32_t)sub * 32u;
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col + (uint32_t)b * 128u +
-                               (uint32_t)sub * 32u,
-                           v);
+        tmem_ld_32x32b_x32(taddr, v);
         tmem_ld_wait();
-        tc_fence_before();
-        warp_arrive(&a1_empty[b], lane);
 
-        const float* bc = b1s + c * kFC + sub * 32;
+        const float4* bc = reinterpret_cast<const float4*>(b1s + c * kFC + sub * 32);
         uint32_t w[16];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float a[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) a[i] = __uint_as_float(v[16 * h + i]) + bc[16 * h + i];
+          for (int i = 0; i < 4; ++i) {
+            const float4 bb = bc[4 * h + i];
+            a[4 * i + 0] = __uint_as_float(v[16 * h + 4 * i + 0]) + bb.x;
+            a[4 * i + 1] = __uint_as_float(v[16 * h + 4 * i + 1]) + bb.y;
+            a[4 * i + 2] = __uint_as_float(v[16 * h + 4 * i + 2]) + bb.z;
+            a[4 * i + 3] = __uint_as_float(v[16 * h + 4 * i + 3]) + bb.w;
+          }
           act_n<16>(act, a);
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[8 * h + i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
         }
-        if (!mbar_wait(h_empty, (uint32_t)(gc & 1) ^ 1u, status, 0x20d, abort_flag)) {
-          ok = false;
-          break;
-        }
-        store_row32_swizzled(sh + (size_t)(sub >> 1) * kSlab, r, (sub & 1) * 4, w);
-        fence_proxy_async_smem();
-        warp_arrive(h_full, lane);
+        // H(c) into the first 16 of this thread's 32 columns of acc1[b].
+        tmem_st_32x32b_x16(taddr, w);
+        tmem_st_wait();
+        tc_fence_before();
+        warp_arrive(&h_full[b], lane);
       }
       if (!ok) break;
 
