@@ -30,9 +30,12 @@
 // biases are staged in shared memory once per expert change).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
-// The epilogue thread that owns fp32 columns [32s, 32s+32) of acc1 writes its
-// 32 bf16 hidden values to columns [32s, 32s+16) of the same buffer, so each
-// 16-wide K step of GEMM2 reads 8 contiguous columns at 32*(k/2) + 8*(k%2).
+// The epilogue produces H(c) in two halves (chunk columns [0, 64) and
+// [64, 128)), each with its own barrier, so GEMM2(c) starts on the first half
+// while the GELU of the second is still running.  Epilogue warp group s owns
+// fp32 columns [64h + 16s, +16) of each half h and writes their 16 bf16
+// values to the first 8 of those columns, so the 16-wide K step k of GEMM2
+// reads 8 contiguous columns at 64*(k/4) + 16*(k%4).
 // Shared memory: X tile (D/64 slabs of 16 KB) + one W1 and one W2 slot of
 // 64 KB each for D=256 (two of 32 KB each for D=128) + biases 5 KB +
 // scheduler 2 KB.
@@ -119,8 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* x_full = empty2 + 2 * P::NSLOT;
   uint64_t* x_empty = x_full + 1;
   uint64_t* a1_full = x_empty + 1;  // [2] GEMM1(c) done -> epilogue
-  uint64_t* h_full = a1_full + 2;    // [2] H(c) written -> MMA
-  uint64_t* a2_full = h_full + 2;
+  uint64_t* h_full = a1_full + 2;    // [2][2] half h of H(c) written -> MMA
+  uint64_t* a2_full = h_full + 4;
   uint64_t* a2_empty = a2_full + 1;
   uint64_t* drain = a2_empty + 1;
   uint64_t* bfree = drain + 1;   // epilogue threads done with the staged biases
@@ -143,10 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&a1_full[i], 1);
-      mbar_init(&h_full[i], kEpiWarps);
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(&a1_full[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&h_full[i], kEpiWarps);
     mbar_init(a2_full, 1);
     mbar_init(a2_empty, kEpiWarps);
     mbar_init(drain, 1);
@@ -204,6 +205,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < P::XK; ++kb)
           tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
         ++x_issued;
+        // The next tile's rows come from HBM; pull them into L2 now so that
+        // their load at the tile boundary does not stall the tensor core.
+        if (t + (int)gridDim.x < total) {
+          const TileCoord nx = sched.decode(t + (int)gridDim.x);
+          for (int kb = 0; kb < P::XK; ++kb) tma_prefetch_l2_2d(&tmX, kb * kBK, nx.row0);
+        }
         for (int s = 0; s < nch + kLag && ok; ++s) {
           if (s < nch) {  // W1 rows [s*128, +128): k-slabs [128 x 64], W1H per half
             ok = load_chunk(ring1, P::W1C, full1, empty1, n1, 0x201,
@@ -295,30 +302,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
             }
-            if (!mbar_wait(&h_full[b], k & 1u, status, 0x209, abort_flag)) {
-              ok = false;
-              break;
-            }
             const int slot = (int)(n2 % P::NSLOT);
             if (!mbar_wait(&full2[slot], (uint32_t)((n2 / P::NSLOT) & 1), status, 0x20a,
                            abort_flag)) {
               ok = false;
               break;
             }
-            tc_fence_after();
             const uint32_t h_tmem = tmem_base + kAcc1Col + (uint32_t)b * 128u;
             const uint32_t b0 = ring2_addr + (uint32_t)(slot * P::W2C);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {  // k-slab h: K columns [64h, 64h+64) of the chunk
+            for (int h = 0; h < 2; ++h) {  // K columns [64h, 64h+64) of the chunk = W2 k-slab h
+              if (!mbar_wait(&h_full[2 * b + h], k & 1u, status, 0x209, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
 #pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk) {
-                const int k16 = h * (kBK / 16) + kk;  // 16-wide K step within the chunk
-                umma_bf16_ts(tmem_base, h_tmem + (uint32_t)((k16 >> 1) * 32 + (k16 & 1) * 8),
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                umma_bf16_ts(tmem_base, h_tmem + (uint32_t)(h * 64 + kk * 16),
                              smem_desc_sw128(b0 + (uint32_t)(h * P::W2H) + kk * 32), idesc2,
                              (c | h | kk) != 0 ? 1u : 0u);
-              }
               umma_commit(&empty2[2 * slot + h]);
             }
+            if (!ok) break;
             ++n2;
             if (c == nch - 1) umma_commit(a2_full);
           }
@@ -367,34 +373,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col +
-                               (uint32_t)b * 128u + (uint32_t)sub * 32u;
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr, v);
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + kAcc1Col +
+                               (uint32_t)b * 128u + (uint32_t)sub * 16u;
+        uint32_t v[2][16];
+        tmem_ld_32x32b_x16(tbase, v[0]);        // columns [16s, +16)
+        tmem_ld_32x32b_x16(tbase + 64u, v[1]);  // columns [64 + 16s, +16)
         tmem_ld_wait();
-
-        const float4* bc = reinterpret_cast<const float4*>(b1s + c * kFC + sub * 32);
-        uint32_t w[16];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
+          const float4* bc = reinterpret_cast<const float4*>(b1s + c * kFC + h * 64 + sub * 16);
           float a[16];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float4 bb = bc[4 * h + i];
-            a[4 * i + 0] = __uint_as_float(v[16 * h + 4 * i + 0]) + bb.x;
-            a[4 * i + 1] = __uint_as_float(v[16 * h + 4 * i + 1]) + bb.y;
-            a[4 * i + 2] = __uint_as_float(v[16 * h + 4 * i + 2]) + bb.z;
-            a[4 * i + 3] = __uint_as_float(v[16 * h + 4 * i + 3]) + bb.w;
+            const float4 bb = bc[i];
+            a[4 * i + 0] = __uint_as_float(v[h][4 * i + 0]) + bb.x;
+            a[4 * i + 1] = __uint_as_float(v[h][4 * i + 1]) + bb.y;
+            a[4 * i + 2] = __uint_as_float(v[h][4 * i + 2]) + bb.z;
+            a[4 * i + 3] = __uint_as_float(v[h][4 * i + 3]) + bb.w;
           }
           act_n<16>(act, a);
+          uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[8 * h + i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
+          for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
+          // Half h of H(c): into the first 8 of this thread's 16 columns.
+          tmem_st_32x32b_x8(tbase + (uint32_t)(h * 64), w);
+          tmem_st_wait();
+          tc_fence_before();
+          warp_arrive(&h_full[2 * b + h], lane);
         }
-        // H(c) into the first 16 of this thread's 32 columns of acc1[b].
-        tmem_st_32x32b_x16(taddr, w);
-        tmem_st_wait();
-        tc_fence_before();
-        warp_arrive(&h_full[b], lane);
       }
       if (!ok) break;
 
