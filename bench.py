@@ -39,12 +39,14 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
 CPU_SAMPLE_TOKENS = 8192
 CALIBRATION_TOKENS = 65536
+CFG4_SAMPLES = 2048
 
 
 def load_peaks():
@@ -561,6 +563,214 @@ def run_ep(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def cfg4_batch(seed: int = 0, samples: int = CFG4_SAMPLES):
+    """Configuration 4: 2048 packed sequences with lengths U{16..256}; every
+    token carries the 28 configuration-3 bags."""
+    from cti_b200 import synth
+
+    lens = synth.packed_lengths(samples, 16, 256, seed)
+    uo = torch.zeros(samples + 1, dtype=torch.int64)
+    uo[1:] = torch.cumsum(torch.from_numpy(lens.astype(np.int64)), 0)
+    T = int(uo[-1])
+    bb = synth.bag_batch(batch=T, seed=seed)
+    return bb, uo, T
+
+
+def init_cfg4_model(model, seed: int = 0):
+    """Random init of the configuration: weights and embedding rows
+    ~N(0, 0.02), biases 0, LayerNorms (1, 0); every router bias gets the
+    configuration-2 Zipf(1.2) profile."""
+    from cti_b200 import synth
+
+    g = torch.Generator().manual_seed(seed + 11)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "rep_encoder.emb" in name:
+                continue
+            if "norm" in name:
+                p.fill_(1.0 if name.endswith("weight") else 0.0)
+            elif p.dim() > 1:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+            else:
+                p.zero_()
+        for i, m in enumerate(model.seq_encoder.moe):
+            m.gate.w_g.bias.copy_(synth.zipf_router_bias(m.num_experts, 1.2, seed + i))
+
+
+def run_e2e(args, world, rank, local):
+    """--config cfg4: the full CTR model forward (pooling -> RepEncoder ->
+    8 x (attention + MoE) -> MLP head) on one packed batch; metric = ms per
+    batch.  Every rank runs its own replica (the model does not shard)."""
+    from cti_b200 import _lib, synth
+    from cti_b200.model import build_ctr_model
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    bb, uo, T = cfg4_batch(seed=rank)
+    model = build_ctr_model(bb.vocab.tolist())
+    init_cfg4_model(model)
+    model.to(dev)
+    model.rep_encoder.emb.weight = torch.nn.Parameter(
+        synth.embedding_table(bb.total_rows, 64, seed=rank, device=dev), requires_grad=False)
+    model.prepare_for_inference()
+    host = {"_flat_values": bb.values, "_flat_row_offsets": bb.row_offsets,
+            "_val_offsets": bb.val_offsets, "user_offsets": uo}
+    batch = {k: v.to(dev) for k, v in host.items()}
+    batch["max_seqlen"] = 256
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    for _ in range(args.warmup):
+        model.predict(batch)
+    torch.cuda.synchronize(dev)
+    _lib.raise_on_status(dev)
+    sampler = ClockSampler(dev) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.start()
+    times = time_steps(lambda: model.predict(batch), args.steps, flush, dev)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    _lib.raise_on_status(dev)
+    step_ms = max_over_ranks(statistics.median(times), world, dev)
+
+    # End to end: pinned host ids/offsets -> device, forward, probabilities -> host.
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    dev_in = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    probs_h = torch.empty(T, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        for k in pinned:
+            dev_in[k].copy_(pinned[k], non_blocking=True)
+        b = dict(dev_in)
+        b["max_seqlen"] = 256
+        probs_h.copy_(model.predict(b), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(statistics.median(time_steps(e2e_step, args.steps, flush, dev,
+                                                         hide_host=False)), world, dev)
+
+    # Stage split of one forward (CUDA events), median of 3.
+    enc = model.seq_encoder
+    stage = {"pool": [], "rep_norm_linear": [], "attention": [], "moe": [], "head": []}
+    from cti_b200.model import ATTENTION
+    for _ in range(3):
+        flush.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4 + 4 * enc.num_layers)]
+        i = 0
+        ev[i].record(); i += 1
+        pooled = model.rep_encoder.pool(batch, out_dtype=torch.bfloat16)
+        ev[i].record(); i += 1
+        x = model.rep_encoder.linear(model.rep_encoder.input_norm(pooled))
+        ev[i].record(); i += 1
+        cu = batch["user_offsets"].to(torch.int32)
+        marks = []
+        H, hd = enc.n_heads, enc.head_dim
+        for l in range(enc.num_layers):
+            e0 = ev[i]; e0.record(); i += 1
+            qkv = enc.qkv_proj[l](enc.norm1[l](x)).view(T, H, 3 * hd)
+            q, k, v = (t.contiguous() for t in torch.split(qkv, hd, dim=-1))
+            a = ATTENTION[enc.attention](q, k, v, cu, 256).reshape(T, enc.d_model)
+            x = x + enc.out_proj[l](a)
+            e1 = ev[i]; e1.record(); i += 1
+            mo, _ = enc.moe[l](enc.norm2[l](x).unsqueeze(0))
+            x = x + mo[0]
+            e2 = ev[i]; e2.record(); i += 1
+            marks.append((e0, e1, e2))
+        torch.sigmoid(torch.clamp(model.linear(x), -15, 15).float())
+        ev[i].record()
+        torch.cuda.synchronize(dev)
+        stage["pool"].append(ev[0].elapsed_time(ev[1]))
+        stage["rep_norm_linear"].append(ev[1].elapsed_time(ev[2]))
+        stage["attention"].append(sum(a.elapsed_time(b) for a, b, c in marks))
+        stage["moe"].append(sum(b.elapsed_time(c) for a, b, c in marks))
+        stage["head"].append(marks[-1][2].elapsed_time(ev[i]))
+    stages = {k: statistics.median(v) for k, v in stage.items()}
+
+    # Roofline of the pooling kernel (HBM gather; the largest single kernel).
+    N = bb.values.numel()
+    pool_bytes = 8 * N + 8 * 28 * (T + 1) + 128 * N + 2 * T * 28 * 64
+    peaks, peak_src = load_peaks()
+    pool_gbs = pool_bytes / (stages["pool"] / 1e3) / 1e9
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_e2e(model, bb, uo, args.cpu_seconds)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    line = {
+        "metric": "e2e_forward_ms_per_batch", "value": step_ms, "unit": "ms/batch",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"cfg4: CTR model forward, {CFG4_SAMPLES} packed sequences "
+                               f"U{{16..256}} ({T} tokens), 28 bags per token, RepEncoder "
+                               "LN(1792)+Linear(1792->256), 8 x (varlen causal attention 8x32 + "
+                               "Top-2 MoE 16 experts d_ff 1024), MLP head 256->128->1",
+                   "tokens": T, "ids": N, "layers": 8, "attention": enc.attention,
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "per_gpu": "one replica"},
+        "e2e": {"value": e2e_ms, "unit": "ms/batch", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": T * 4},
+        "roofline": {"bound": "hbm", "kernel": "embbag_kernel<64, bf16> (pooling)",
+                     "achieved": pool_gbs, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                     "frac": pool_gbs / float(peaks["hbm_gbs"]),
+                     "peak_source": f"hbm_gbs of {peak_src}", "bytes_per_launch": pool_bytes,
+                     "traffic": None},
+        "stages_ms": stages,
+        "tokens_per_s": T / (step_ms / 1e3),
+        "gpu_launches": (1 + 5 * enc.num_layers) * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_e2e(model, bb, uo, seconds: float, sample_seqs: int = 2):
+    """The oracle (fp32 CPU restatement of the reference model) on the first
+    `sample_seqs` sequences of the batch, scaled to the whole batch by
+    tokens."""
+    from oracle import e2e_ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    T = int(uo[-1])
+    t_s = int(uo[sample_seqs])
+    F_ = 28
+    offs = bb.row_offsets.view(F_, T + 1)[:, :t_s + 1]
+    vals, voff = [], []
+    start = 0
+    for f in range(F_):
+        v0 = int(bb.val_offsets[f])
+        n = int(offs[f, -1])
+        vals.append(bb.values[v0:v0 + n])
+        voff.append(start)
+        start += n
+    batch = {"_flat_values": torch.cat(vals), "_flat_row_offsets": offs.reshape(-1).clone(),
+             "_val_offsets": torch.tensor(voff, dtype=torch.int64),
+             "user_offsets": uo[:sample_seqs + 1].clone()}
+    sd = {k: v.detach().float().cpu() for k, v in model.state_dict().items()}
+    kw = dict(slot_num=28, n_heads=8, num_layers=8, num_experts=16,
+              table_row_base=bb.table_row_base, vocab=bb.vocab)
+    e2e_ref.ctr_forward_ref(sd, batch, **kw)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        e2e_ref.ctr_forward_ref(sd, batch, **kw)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 1000:
+            break
+    per_call = el / n
+    return {"value": per_call * (T / t_s) * 1e3, "unit": "ms/batch",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample_seqs} of {CFG4_SAMPLES} sequences ({t_s} of {T} tokens), "
+                      f"{n} calls ({el:.1f} s), scaled to the batch by tokens; fp32, "
+                      "oracle/e2e_ref.py (baseline/infer.py:244-439)"}
+
+
 def run_profile_workload(args):
     """--profile STAGE: the configuration-2 workload with one stage launched
     warmup + steps times and nothing else timed; the small, self-contained
@@ -678,8 +888,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg5"],
+    ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
                     help="cfg2: MoE layer (default, the headline); cfg3: embedding bag; "
+                         "cfg4: full CTR model forward (ms per batch); "
                          "cfg5: expert-parallel MoE layer (strong scaling over N)")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="cfg5 expert placement over the ranks")
@@ -705,6 +916,8 @@ def main():
             run_embbag(args, world, rank, local)
         elif args.config == "cfg5":
             run_ep(args, world, rank, local)
+        elif args.config == "cfg4":
+            run_e2e(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

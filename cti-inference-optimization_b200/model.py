@@ -1,0 +1,192 @@
+"""The CTR model around the hot path (the 8-layer forward of configuration 4).
+
+Drop-ins for ``TransformerEncoder`` and ``CTRModel`` of ``baseline/infer.py``
+(:360-439; the same graph runs in ``online_best/infer.py:2440-2620``), with
+the reference's parameter names, so a reference state dict loads as is:
+
+  * ``rep_encoder``: the ``RepEncoder`` drop-in (sm_100a pooling kernel,
+    then LayerNorm over slot_num*emb_dim, then Linear - the reference order,
+    ``baseline/infer.py:263-265``);
+  * ``seq_encoder``: pre-LN layers, each
+        x = x + out_proj(attention(qkv_proj(norm1(x))))
+        x = x + moe(norm2(x))
+    with the reference's interleaved per-head qkv layout (``qkv.view(T, H,
+    3*head_dim)`` then split into q, k, v; ``baseline/infer.py:391-395``),
+    causal attention inside each packed sequence, and the ``SMoE`` drop-in
+    (sm_100a router, dispatch, fused expert FFN, combine).  ``ffn1`` /
+    ``ffn2`` exist in the reference but are never called; they are kept so
+    that state dicts match;
+  * the head: the configuration's MLP d_model -> 128 -> 1 (ReLU between)
+    under the reference's attribute name ``linear``, then clamp(+-15) as in
+    ``baseline/infer.py:437``; ``predict`` applies the sigmoid
+    (``baseline/infer.py:686``).
+
+Attention over the packed sequences calls PyTorch's variable-length flash
+attention (``torch.nn.attention.varlen.varlen_attn``) with a causal window;
+the reference builds a dense [T, T] mask instead (``get_sequence_causal_mask``,
+``baseline/infer.py:420-427``), which does not fit at T = 278k.  This module
+is the model around the hot path; the hot path itself is the MoE layer and
+the pooling.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from .embedding import RepEncoder
+from .moe import SMoE
+
+
+def varlen_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
+    """Causal attention inside each packed sequence.  q, k, v [T, H, hd]
+    (bf16, CUDA); cu_seqlens int32 [N+1]."""
+    from torch.nn.attention.varlen import varlen_attn
+
+    return varlen_attn(q, k, v, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen,
+                       window_size=(-1, 0))
+
+
+def padded_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
+    """The same through scaled_dot_product_attention on sequences padded to
+    max_seqlen.  Padding sits after each sequence's last token, so the
+    causal mask alone keeps it out of every real query."""
+    T, H, hd = q.shape
+    N = cu_seqlens.numel() - 1
+    starts = cu_seqlens[:-1].long()
+    lens = (cu_seqlens[1:] - cu_seqlens[:-1]).long()
+    seq = torch.repeat_interleave(torch.arange(N, device=q.device), lens)
+    pos = torch.arange(T, device=q.device) - starts[seq]
+
+    def pad(t):
+        out = t.new_zeros(N, max_seqlen, H, hd)
+        out[seq, pos] = t
+        return out.transpose(1, 2)
+
+    o = torch.nn.functional.scaled_dot_product_attention(pad(q), pad(k), pad(v), is_causal=True)
+    return o.transpose(1, 2)[seq, pos]
+
+
+ATTENTION = {"varlen": varlen_causal_attention, "padded": padded_causal_attention}
+
+
+class TransformerEncoder(nn.Module):
+    """``TransformerEncoder`` of ``baseline/infer.py:360-411`` with the MoE
+    drop-in.  ``forward(x [T, D] or [1, T, D], extension)`` where
+    ``extension`` holds ``cu_seqlens`` (int32 [N+1]) and ``max_seqlen``."""
+
+    def __init__(self, d_model: int, n_heads: int, num_layers: int, dim_ff: int,
+                 num_experts: int = 8, activation: str = "gelu", renormalize: bool = True,
+                 attention: str = "varlen"):
+        super().__init__()
+        if d_model % n_heads:
+            raise ValueError("d_model must be a multiple of n_heads")
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.num_layers = num_layers
+        self.qkv_proj = nn.ModuleList([nn.Linear(d_model, 3 * d_model) for _ in range(num_layers)])
+        self.out_proj = nn.ModuleList([nn.Linear(d_model, d_model) for _ in range(num_layers)])
+        self.ffn1 = nn.ModuleList([nn.Linear(d_model, dim_ff) for _ in range(num_layers)])
+        self.ffn2 = nn.ModuleList([nn.Linear(dim_ff, d_model) for _ in range(num_layers)])
+        self.norm1 = nn.ModuleList([nn.LayerNorm(d_model) for _ in range(num_layers)])
+        self.norm2 = nn.ModuleList([nn.LayerNorm(d_model) for _ in range(num_layers)])
+        self.moe = nn.ModuleList([
+            SMoE(d_model, dim_ff, num_experts, k=2, activation=activation,
+                 renormalize=renormalize)
+            for _ in range(num_layers)
+        ])
+        self.attention = attention
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor, extension: dict):
+        squeeze = x.dim() == 3
+        x = x.reshape(-1, self.d_model)
+        cu = extension["cu_seqlens"]
+        max_len = int(extension["max_seqlen"])
+        attn = ATTENTION[self.attention]
+        T = x.shape[0]
+        H, hd = self.n_heads, self.head_dim
+        for i in range(self.num_layers):
+            residual = x
+            qkv = self.qkv_proj[i](self.norm1[i](x)).view(T, H, 3 * hd)
+            q, k, v = (t.contiguous() for t in torch.split(qkv, hd, dim=-1))
+            a = attn(q, k, v, cu, max_len).reshape(T, self.d_model)
+            x = residual + self.out_proj[i](a)
+            moe_out, _ = self.moe[i](self.norm2[i](x).unsqueeze(0))
+            x = x + moe_out[0]
+        return (x.unsqueeze(0) if squeeze else x), None
+
+
+class CTRModel(nn.Module):
+    """``CTRModel`` of ``baseline/infer.py:414-439`` with the configuration's
+    MLP head.  ``forward(batch)`` reads the flat pooling layout plus
+    ``user_offsets`` (int64 [N+1], token offsets of the packed sequences)
+    and returns ``(logits [T, 1] clamped to +-15, None)``."""
+
+    def __init__(self, rep_encoder: RepEncoder, seq_encoder: TransformerEncoder, d_model: int,
+                 head_hidden: int = 128):
+        super().__init__()
+        self.rep_encoder = rep_encoder
+        self.seq_encoder = seq_encoder
+        self.d_model = d_model
+        self.linear = nn.Sequential(nn.Linear(d_model, head_hidden), nn.ReLU(),
+                                    nn.Linear(head_hidden, 1))
+
+    @torch.no_grad()
+    def prepare_for_inference(self, dtype: torch.dtype = torch.bfloat16) -> "CTRModel":
+        """Casts the model to ``dtype`` for inference, except the routers,
+        which stay fp32 (the fp32 router of the MoE layer).  The embedding
+        tables are fp16, the pooling kernel's input type."""
+        # Take the table and the routers out while the rest is cast, so that
+        # their values never pass through `dtype`.
+        emb = self.rep_encoder.emb
+        self.rep_encoder.emb = None
+        gates = [m.gate for m in self.seq_encoder.moe]
+        for m in self.seq_encoder.moe:
+            m.gate = None
+        self.to(dtype)
+        self.rep_encoder.emb = emb.half()
+        for m, g in zip(self.seq_encoder.moe, gates):
+            m.gate = g.float()
+            m.prepare_for_inference()
+        return self
+
+    @staticmethod
+    def sequence_info(batch: dict, device) -> tuple[torch.Tensor, int]:
+        uo = batch["user_offsets"]
+        cu = uo.to(device=device, dtype=torch.int32, non_blocking=True)
+        if "max_seqlen" in batch:
+            max_len = int(batch["max_seqlen"])
+        else:
+            max_len = int((uo[1:] - uo[:-1]).max())
+        return cu, max_len
+
+    @torch.no_grad()
+    def forward(self, batch: dict):
+        dev = self.linear[0].weight.device
+        cu, max_len = self.sequence_info(batch, dev)
+        x = self.rep_encoder(batch)
+        h, _ = self.seq_encoder(x, {"cu_seqlens": cu, "max_seqlen": max_len})
+        logits = torch.clamp(self.linear(h), min=-15.0, max=15.0)
+        return logits, None
+
+    @torch.no_grad()
+    def predict(self, batch: dict) -> torch.Tensor:
+        """CTR probabilities [T] (fp32)."""
+        logits, _ = self.forward(batch)
+        return torch.sigmoid(logits.float()).reshape(-1)
+
+
+def build_ctr_model(vocab_sizes, emb_dim: int = 64, slot_num: int = 28, d_model: int = 256,
+                    n_heads: int = 8, num_layers: int = 8, dim_ff: int = 1024,
+                    num_experts: int = 16, head_hidden: int = 128,
+                    attention: str = "varlen") -> CTRModel:
+    """The configuration-4 model: per-slot tables, 8 layers of 8 heads x 32,
+    16 experts of d_ff 1024, MLP head 256 -> 128 -> 1."""
+    rep = RepEncoder(vocab_size=int(sum(vocab_sizes)), emb_dim=emb_dim, padding_idx=0,
+                     slot_num=slot_num, d_model=d_model, vocab_sizes=vocab_sizes)
+    enc = TransformerEncoder(d_model, n_heads, num_layers, dim_ff, num_experts,
+                             attention=attention)
+    return CTRModel(rep, enc, d_model, head_hidden)

@@ -18,6 +18,12 @@ What runs:
     linear replaced by identities, so forward() returns the pooled
     [B, 28*64] tensor.  Per-feature tables run one single-slot RepEncoder
     per feature.
+  * baseline/infer.py CTRModel (RepEncoder -> TransformerEncoder with its
+    SMoE layers -> head, :244-439) in fp32 on CPU, eval mode, at a small
+    size: the SMoE experts and gates patched as for the "config" fixtures,
+    and CTRModel.linear replaced by the configuration's MLP head
+    (d -> 128 -> 1, ReLU).  The attention is the reference's own
+    scaled_dot_product with its dense causal sequence mask.
 Each fixture stores the outputs plus the SHA-256 of the inputs
 (tests/golden/golden_inputs.py regenerates the inputs from seeds).
 """
@@ -128,6 +134,37 @@ def make_bags(ref, per_feature: bool):
                         input_sha256=np.array(digest))
 
 
+def make_e2e(ref, name: str):
+    batch, sd = gi.e2e_inputs(name)
+    N, Lmax, D, H, L, Fd, E, V, _ = gi.E2E_CASES[name]
+    rep = ref.RepEncoder(vocab_size=V, emb_dim=gi.E2E_EMB, padding_idx=0, slot_num=gi.E2E_SLOTS,
+                         d_model=D)
+    enc = ref.TransformerEncoder(D, H, L, Fd)
+    model = ref.CTRModel(rep, enc, D)
+    model.linear = nn.Sequential(nn.Linear(D, gi.E2E_HEAD), nn.ReLU(), nn.Linear(gi.E2E_HEAD, 1))
+    model.load_state_dict(sd, strict=True)
+    model.eval()
+    for moe in enc.moe:
+        assert moe.num_experts == E
+        for ex in moe.experts:
+            ex.forward = types.MethodType(_gelu_expert_forward, ex)
+        moe.gate.forward = types.MethodType(_stable_renorm_gate_forward, moe.gate)
+    T = int(batch["user_offsets"][-1])
+    ref_batch = {"user_offsets": batch["user_offsets"]}
+    for f in range(gi.E2E_SLOTS):
+        offs = batch["_flat_row_offsets"][f * (T + 1):(f + 1) * (T + 1)]
+        v0 = int(batch["_val_offsets"][f])
+        ref_batch[f + 1] = (batch["_flat_values"][v0:v0 + int(offs[-1])], offs)
+    hidden = {}
+    enc.register_forward_hook(lambda mod, inp, out: hidden.__setitem__("h", out[0]))
+    with torch.no_grad():
+        logits, _ = model(ref_batch)
+        probs = torch.sigmoid(logits)
+    np.savez_compressed(HERE / f"{name}.npz", hidden=hidden["h"].reshape(T, D).numpy(),
+                        logits=logits.reshape(-1).numpy(), probs=probs.reshape(-1).numpy(),
+                        input_sha256=np.array(gi.e2e_digest(batch, sd)))
+
+
 def main() -> None:
     ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "../reference")
     ref = load_reference(ref_root)
@@ -136,6 +173,8 @@ def main() -> None:
         make_moe(ref, name)
     make_bags(ref, per_feature=False)
     make_bags(ref, per_feature=True)
+    for name in gi.E2E_CASES:
+        make_e2e(ref, name)
     keys = list(ref.SMoE(128, 256, 4).state_dict().keys())
     keys += list(ref.RepEncoder(100, 8, 0, 28, 16).state_dict().keys())
     (HERE / "reference_state_dict_keys.txt").write_text("\n".join(keys) + "\n")

@@ -1,0 +1,126 @@
+"""The configuration-4 model on the B200 (bf16; sm_100a pooling and MoE
+kernels, library attention) against the reference CTRModel fixture and the
+CPU oracle.  Tolerances: CTR probabilities within 1e-3 absolute (the
+north-star bound), encoder output within max rel err 2e-2 (bf16 vs fp32)."""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+from helpers import MOE_MAX_REL_ERR, load_golden, max_rel_err
+from oracle import e2e_ref
+
+pytestmark = pytest.mark.gpu
+STRESS_MAX_REL_ERR = 5e-2
+
+
+def _build(name, dev, attention):
+    import cti_b200
+    from cti_b200.model import CTRModel, TransformerEncoder
+
+    N, Lmax, D, H, L, Fd, E, V, _ = gi.E2E_CASES[name]
+    rep = cti_b200.RepEncoder(vocab_size=V, emb_dim=gi.E2E_EMB, padding_idx=0,
+                              slot_num=gi.E2E_SLOTS, d_model=D)
+    enc = TransformerEncoder(D, H, L, Fd, num_experts=E, attention=attention)
+    model = CTRModel(rep, enc, D, head_hidden=gi.E2E_HEAD)
+    batch, sd = gi.e2e_inputs(name)
+    model.load_state_dict(sd, strict=True)
+    model.to(dev).prepare_for_inference()
+    return model, batch, sd
+
+
+@pytest.mark.parametrize("attention", ["varlen", "padded"])
+@pytest.mark.parametrize("name", list(gi.E2E_CASES))
+def test_ctr_model_matches_reference_fixture(cuda_device, attention, name):
+    """Configuration init (weight std 0.02): encoder output within max rel
+    err 2e-2 and probabilities within 1e-3 absolute.
+    Large-weight stress case (weights 2.5-5x the configuration's, logits of
+    several units): two layers of bf16 activations against fp32 put the
+    encoder output and the logits within max rel err 5e-2 (measured 2.9e-2),
+    not 1e-3 in probability."""
+    from cti_b200 import _lib
+
+    model, batch, sd = _build(name, cuda_device, attention)
+    gold = load_golden(name)
+    assert str(gold["input_sha256"]) == gi.e2e_digest(batch, sd)
+    hidden = {}
+    model.seq_encoder.register_forward_hook(lambda m, i, o: hidden.__setitem__("h", o[0]))
+    logits, aux = model(batch)
+    probs = model.predict(batch)
+    _lib.raise_on_status(cuda_device)
+    T = int(batch["user_offsets"][-1])
+    assert aux is None and logits.shape == (T, 1)
+    assert probs.shape == (T,) and probs.dtype == torch.float32
+    assert model.seq_encoder.moe[0].gate.w_g.weight.dtype == torch.float32  # fp32 router
+    init_scale = gi.E2E_CASES[name][-1] is not None
+    tol = MOE_MAX_REL_ERR if init_scale else STRESS_MAX_REL_ERR
+    assert max_rel_err(hidden["h"].float().cpu(), torch.from_numpy(gold["hidden"])) < tol
+    if init_scale:
+        np.testing.assert_allclose(probs.cpu().numpy(), gold["probs"], rtol=0, atol=1e-3)
+    else:
+        assert max_rel_err(logits.float().reshape(-1).cpu(), torch.from_numpy(gold["logits"])) < tol
+
+
+def test_ctr_model_attention_backends_agree(cuda_device):
+    """varlen flash attention and padded SDPA on a larger packed batch."""
+    from cti_b200.model import padded_causal_attention, varlen_causal_attention
+
+    g = torch.Generator().manual_seed(3)
+    lens = torch.randint(1, 257, (64,), generator=g)
+    cu = torch.zeros(65, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    T = int(cu[-1])
+    q, k, v = (torch.randn(T, 8, 32, generator=g).bfloat16().to(cuda_device) for _ in range(3))
+    cu = cu.to(cuda_device)
+    a = varlen_causal_attention(q, k, v, cu, 256).float()
+    b = padded_causal_attention(q, k, v, cu, 256).float()
+    assert max_rel_err(a, b) < 1e-2
+    # one sequence against a plain fp32 softmax
+    s0, s1 = int(cu[5]), int(cu[6])
+    qs, ks, vs = (t[s0:s1].float().transpose(0, 1) for t in (q, k, v))
+    sc = (qs @ ks.transpose(-1, -2)) / 32 ** 0.5
+    sc = sc.masked_fill(~torch.ones(s1 - s0, s1 - s0, dtype=torch.bool, device=cuda_device).tril(),
+                        float("-inf"))
+    ref = (torch.softmax(sc, -1) @ vs).transpose(0, 1)
+    assert max_rel_err(a[s0:s1], ref) < 1e-2
+
+
+def test_cfg4_shaped_model_matches_oracle(cuda_device):
+    """The configuration-4 architecture and init (D 256, 8 heads x 32, 16
+    experts of d_ff 1024 with the Zipf router bias, per-slot tables, weights
+    ~N(0, 0.02)) at 2 layers and 24 sequences, against the oracle:
+    probabilities within 1e-3 absolute."""
+    import sys
+    from pathlib import Path
+
+    from cti_b200 import _lib, synth
+    from cti_b200.model import build_ctr_model
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+
+    nseq = 24
+    lens = torch.randint(16, 257, (nseq,), generator=torch.Generator().manual_seed(1))
+    uo = torch.zeros(nseq + 1, dtype=torch.long)
+    uo[1:] = torch.cumsum(lens, 0)
+    T = int(uo[-1])
+    bb = synth.bag_batch(batch=T, seed=2, vocab_lo=1e3, vocab_hi=2e4)
+    model = build_ctr_model(bb.vocab.tolist(), num_layers=2)
+    bench.init_cfg4_model(model)
+    with torch.no_grad():
+        model.rep_encoder.emb.weight.copy_(synth.embedding_table(bb.total_rows, 64, seed=2).float())
+        for name, p in model.named_parameters():
+            if "gate" not in name and "emb" not in name:
+                p.copy_(p.bfloat16().float())
+    sd = {k: v.clone() for k, v in model.state_dict().items()}
+    batch = {"_flat_values": bb.values, "_flat_row_offsets": bb.row_offsets,
+             "_val_offsets": bb.val_offsets, "user_offsets": uo}
+    model.to(cuda_device).prepare_for_inference()
+    logits, _ = model(batch)
+    probs = model.predict(batch)
+    _lib.raise_on_status(cuda_device)
+    torch.set_num_threads(8)
+    _, ref_logits, ref = e2e_ref.ctr_forward_ref(sd, batch, slot_num=28, n_heads=8, num_layers=2,
+                                                 num_experts=16, table_row_base=bb.table_row_base,
+                                                 vocab=bb.vocab)
+    np.testing.assert_allclose(probs.cpu().numpy(), ref.numpy(), rtol=0, atol=1e-3)
