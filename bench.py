@@ -601,7 +601,7 @@ def run_e2e(args, world, rank, local):
     """--config cfg4: the full CTR model forward (pooling -> RepEncoder ->
     8 x (attention + MoE) -> MLP head) on one packed batch; metric = ms per
     batch.  Every rank runs its own replica (the model does not shard)."""
-    from cti_b200 import _lib, synth
+    from cti_b200 import _lib, ops, synth
     from cti_b200.model import build_ctr_model
 
     dev = torch.device("cuda", local)
@@ -657,38 +657,32 @@ def run_e2e(args, world, rank, local):
     # Stage split of one forward (CUDA events), median of 3.
     enc = model.seq_encoder
     stage = {"pool": [], "rep_norm_linear": [], "attention": [], "moe": [], "head": []}
-    from cti_b200.model import ATTENTION
     for _ in range(3):
         flush.zero_()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4 + 4 * enc.num_layers)]
-        i = 0
-        ev[i].record(); i += 1
+        evs = []
+
+        def mark(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append((name, e))
+
+        mark("start")
         pooled = model.rep_encoder.pool(batch, out_dtype=torch.bfloat16)
-        ev[i].record(); i += 1
-        x = model.rep_encoder.linear(model.rep_encoder.input_norm(pooled))
-        ev[i].record(); i += 1
+        mark("pool")
+        _, normed = ops.add_layernorm(pooled, None, model.rep_encoder.input_norm.weight,
+                                      model.rep_encoder.input_norm.bias)
+        x = model.rep_encoder.linear(normed)
+        mark("rep_norm_linear")
         cu = batch["user_offsets"].to(torch.int32)
-        marks = []
-        H, hd = enc.n_heads, enc.head_dim
-        for l in range(enc.num_layers):
-            e0 = ev[i]; e0.record(); i += 1
-            qkv = enc.qkv_proj[l](enc.norm1[l](x)).view(T, H, 3 * hd)
-            q, k, v = (t.contiguous() for t in torch.split(qkv, hd, dim=-1))
-            a = ATTENTION[enc.attention](q, k, v, cu, 256).reshape(T, enc.d_model)
-            x = x + enc.out_proj[l](a)
-            e1 = ev[i]; e1.record(); i += 1
-            mo, _ = enc.moe[l](enc.norm2[l](x).unsqueeze(0))
-            x = x + mo[0]
-            e2 = ev[i]; e2.record(); i += 1
-            marks.append((e0, e1, e2))
-        torch.sigmoid(torch.clamp(model.linear(x), -15, 15).float())
-        ev[i].record()
+        h, _ = enc(x, {"cu_seqlens": cu, "max_seqlen": 256, "mark": mark})
+        torch.sigmoid(torch.clamp(model.linear(h), -15, 15).float())
+        mark("head")
         torch.cuda.synchronize(dev)
-        stage["pool"].append(ev[0].elapsed_time(ev[1]))
-        stage["rep_norm_linear"].append(ev[1].elapsed_time(ev[2]))
-        stage["attention"].append(sum(a.elapsed_time(b) for a, b, c in marks))
-        stage["moe"].append(sum(b.elapsed_time(c) for a, b, c in marks))
-        stage["head"].append(marks[-1][2].elapsed_time(ev[i]))
+        acc = {k: 0.0 for k in stage}
+        for (_, a), (name, b) in zip(evs[:-1], evs[1:]):
+            acc[name] += a.elapsed_time(b)
+        for k in stage:
+            stage[k].append(acc[k])
     stages = {k: statistics.median(v) for k, v in stage.items()}
 
     # Roofline of the pooling kernel (HBM gather; the largest single kernel).
@@ -723,7 +717,7 @@ def run_e2e(args, world, rank, local):
                      "traffic": None},
         "stages_ms": stages,
         "tokens_per_s": T / (step_ms / 1e3),
-        "gpu_launches": (1 + 5 * enc.num_layers) * args.steps,
+        "gpu_launches": (2 + 7 * enc.num_layers) * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }

@@ -78,4 +78,9 @@ class RepEncoder(nn.Module):
 
     def forward(self, batch: dict) -> torch.Tensor:
         pooled = self.pool(batch, out_dtype=self.input_norm.weight.dtype)
-        return self.linear(self.input_norm(pooled))
+        if pooled.dtype == torch.bfloat16 and pooled.shape[1] % 256 == 0:
+            _, normed = ops.add_layernorm(pooled, None, self.input_norm.weight,
+                                          self.input_norm.bias, self.input_norm.eps)
+        else:
+            normed = self.input_norm(pooled)
+        return self.linear(normed)

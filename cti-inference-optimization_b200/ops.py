@@ -201,3 +201,28 @@ def embedding_bag_sum(
         "cti_embbag_sum",
     )
     return out
+
+
+def add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor,
+                  bias: torch.Tensor, eps: float = 1e-5, write_sum: bool = True):
+    """The CTR model's residual add + LayerNorm: s = x + residual (bf16), out =
+    LayerNorm(s).  Returns (s, out); s is x itself when residual is None.
+    x, residual [rows, cols] bf16; weight, bias [cols] bf16."""
+    require_cuda(x, "x", torch.bfloat16)
+    if residual is not None:
+        require_cuda(residual, "residual", torch.bfloat16)
+        if residual.shape != x.shape:
+            raise ValueError("x and residual must have the same shape")
+    require_cuda(weight, "weight", torch.bfloat16)
+    require_cuda(bias, "bias", torch.bfloat16)
+    cols = x.shape[-1]
+    rows = x.numel() // cols if cols else 0
+    dev = x.device
+    out = torch.empty_like(x)
+    s = torch.empty_like(x) if (residual is not None and write_sum) else None
+    check(
+        lib.cti_add_layernorm(ptr(x), ptr(residual), ptr(weight), ptr(bias), rows, cols,
+                              float(eps), ptr(s), ptr(out), stream_handle(dev)),
+        "cti_add_layernorm",
+    )
+    return (x if residual is None else s), out

@@ -203,6 +203,22 @@ int cti_embbag_sum(const int64_t* values, int64_t n_values, const int64_t* row_o
                    const int64_t* vocab, const void* table_f16, int64_t table_rows, int64_t B,
                    int F, int dim, void* out, int out_dtype, int32_t* status, void* stream);
 
+/* ----------------------------------------------------------------------
+ * Residual add + LayerNorm of the CTR model around the MoE layer: the
+ * pre-LN steps of TransformerEncoder.forward (baseline/infer.py:388-409,
+ * `residual + y` then nn.LayerNorm) and the RepEncoder LayerNorm over the
+ * pooled 28*64 columns (baseline/infer.py:264).
+ *   s   = bf16(x + residual)   (residual may be NULL: s = x); written to
+ *                              sum if sum is not NULL (needs residual)
+ *   out = bf16((s - mean) * rsqrt(var + eps) * gamma + beta), fp32 mean and
+ *         biased variance of the bf16 row s
+ * bf16 [rows, cols] row-major, gamma / beta bf16 [cols]; cols a multiple of
+ * 256, at most 2048; every pointer 16-byte aligned.
+ * ---------------------------------------------------------------------- */
+int cti_add_layernorm(const void* x_bf16, const void* residual_bf16, const void* gamma_bf16,
+                      const void* beta_bf16, int64_t rows, int cols, float eps, void* sum_bf16,
+                      void* out_bf16, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
