@@ -11,12 +11,15 @@
 //
 // The logits of a 128-token block are a [128 x D] x [D x E] fp32 product,
 // computed as a register-tiled SGEMM: each thread owns a 4-token x 4-expert
-// tile (16 independent chains) and, per d, reads one float4 of activations
-// and one float4 of weights from shared memory - two conflict-free loads per
-// 16 FMAs, so the kernel is bound by the FMA pipe rather than by shared
-// memory.  Activations and router weights are staged 32 d at a time
-// (activations converted to fp32, both d-major), and the global loads of the
-// next step are in flight while the current step's FMAs run.
+// tile (16 independent chains): tokens tg + 32i and experts eg + EG*j, so
+// the 8 (or 2) token rows and 4 (or 16) expert rows a warp reads at once are
+// consecutive rows, which the 16-byte row padding spreads over the banks.  Activations (bf16, [token][d]) and router
+// weights (fp32, [expert][d]) stream through a kStages-deep ring of
+// shared-memory stages, kDC d-values each, filled with cp.async straight
+// from global memory: coalesced row segments, no register staging, and
+// kStages-1 steps of loads in flight while a step is multiplied.  Per 4
+// d-values a thread reads 4 x 8 bytes of activations and 4 x 16 bytes of
+// weights (padded rows, conflict-free) for 64 FMAs.
 //
 // The block also produces the dispatch metadata: for each of its 128 tokens
 // the rank of each route among the block's earlier routes to the same expert
@@ -27,19 +30,36 @@ namespace cti {
 namespace {
 
 constexpr int kTok = CTI_ROUTER_BLOCK_TOKENS;  // 128 tokens per block
-constexpr int kDC = 32;                        // d-values staged per step
+constexpr int kDC = 32;                        // d-values per stage
+constexpr int kStages = 4;
+constexpr int kXPitch = kDC * 2 + 16;          // bytes per token row of a stage (padded)
+constexpr int kWPitch = kDC * 4 + 16;          // bytes per expert row of a stage (padded)
 
 template <int EMAX>
 struct RouterSmem {
-  static constexpr int kStage = kDC * kTok + kDC * EMAX;
-  static constexpr int kLogits = kTok * (EMAX + 1);
-  static constexpr int kFloats = kStage > kLogits ? kStage : kLogits;
-  static constexpr size_t kBytes = (size_t)kFloats * 4 + (size_t)(1 + kTok / 32) * EMAX * 4;
+  static constexpr size_t kXStage = (size_t)kTok * kXPitch;
+  static constexpr size_t kWStage = (size_t)EMAX * kWPitch;
+  static constexpr size_t kRing = kStages * (kXStage + kWStage);
+  static constexpr size_t kLogits = (size_t)kTok * (EMAX + 1) * 4;
+  static constexpr size_t kMain = kRing > kLogits ? kRing : kLogits;
+  static constexpr size_t kBytes = kMain + (size_t)(1 + kTok / 32) * EMAX * 4;
 };
 
 template <int EMAX>
 constexpr int router_threads() {
   return 8 * EMAX < kTok ? kTok : 8 * EMAX;
+}
+
+// 16-byte global -> shared copy; src_bytes = 0 fills the destination with zeros.
+CTI_DEVICE void cp_async16(void* smem_dst, const void* gmem_src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(src_bytes)
+               : "memory");
+}
+CTI_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CTI_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 template <int EMAX>
@@ -48,21 +68,20 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
     const float* __restrict__ bg, int64_t T, int D, int E, int renorm,
     int32_t* __restrict__ idx2, float* __restrict__ gate2, int32_t* __restrict__ route_rank,
     int32_t* __restrict__ block_hist) {
+  using SM = RouterSmem<EMAX>;
   constexpr int EG = EMAX / 4;       // expert groups of 4
   constexpr int NG = 32 * EG;        // GEMM threads: 32 token groups x EG expert groups
   constexpr int NT = NG < kTok ? kTok : NG;  // at least one thread per token
-  // Dynamic shared memory: xs[kDC][kTok] and ws[kDC][EMAX] while the
-  // logits are accumulated, then reused as lg[kTok][EMAX + 1]; then cnt[EMAX]
-  // (block counts) and the per-warp counts [kTok/32][EMAX].
-  extern __shared__ __align__(16) float smem_f[];
-  float (*xs)[kTok] = reinterpret_cast<float (*)[kTok]>(smem_f);
-  float (*ws)[EMAX] = reinterpret_cast<float (*)[EMAX]>(smem_f + kDC * kTok);
-  float (*lg)[EMAX + 1] = reinterpret_cast<float (*)[EMAX + 1]>(smem_f);
-  int* cnt = reinterpret_cast<int*>(smem_f + RouterSmem<EMAX>::kFloats);
+  // Dynamic shared memory: the stage ring while the logits are accumulated,
+  // then reused as lg[kTok][EMAX + 1]; then cnt[EMAX] (block counts) and the
+  // per-warp counts [kTok/32][EMAX].
+  extern __shared__ __align__(16) uint8_t smem_b[];
+  float (*lg)[EMAX + 1] = reinterpret_cast<float (*)[EMAX + 1]>(smem_b);
+  int* cnt = reinterpret_cast<int*>(smem_b + SM::kMain);
 
   const int tid = threadIdx.x;
-  const int eg = tid % EG;   // experts 4*eg .. 4*eg+3
-  const int tg = tid / EG;   // tokens  4*tg .. 4*tg+3
+  const int eg = tid % EG;   // experts eg + EG*j, j = 0..3
+  const int tg = tid / EG;   // tokens  tg + 32*i, i = 0..3
   const bool gemm = tid < NG;
   const int64_t t0 = (int64_t)blockIdx.x * kTok;
 
@@ -72,96 +91,82 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-  // x chunks are prefetched into registers one step ahead: chunk c of a
-  // d-step is token c % 128, 8-wide d-part c / 128 (consecutive lanes store
-  // consecutive tokens in shared memory).
-  constexpr int kXChunks = kTok * (kDC / 8);                   // 512 per step
-  constexpr int kXPerThread = (kXChunks + NT - 1) / NT;
-  constexpr int kWChunks = EMAX * (kDC / 4);                   // float4s of wg per step
-  constexpr int kWPerThread = (kWChunks + NT - 1) / NT;
-  uint4 xpre[kXPerThread];
-  float4 wpre[kWPerThread];
-  auto load_step = [&](int d0) {
-    const int dc = min(kDC, D - d0);
-#pragma unroll
-    for (int q = 0; q < kXPerThread; ++q) {
-      const int c = tid + q * NT;
-      const int tok = c % kTok;
-      const int part = c / kTok;
-      xpre[q] = (c < kXChunks && part * 8 < dc && t0 + tok < T)
-                    ? __ldg(reinterpret_cast<const uint4*>(x + (t0 + tok) * D + d0) + part)
-                    : make_uint4(0, 0, 0, 0);
+  // Stage s of the ring: x part [kTok][kXPitch] bytes, then w part
+  // [EMAX][kWPitch] bytes.  Step k covers d in [k*kDC, k*kDC + kDC).
+  auto x_stage = [&](int s) { return smem_b + (size_t)s * (SM::kXStage + SM::kWStage); };
+  auto w_stage = [&](int s) { return x_stage(s) + SM::kXStage; };
+  const int nsteps = (D + kDC - 1) / kDC;
+  auto issue = [&](int k) {
+    const int d0 = k * kDC;
+    const int dc = min(kDC, D - d0);  // a multiple of 8
+    uint8_t* xs = x_stage(k % kStages);
+    uint8_t* ws = w_stage(k % kStages);
+    constexpr int kXParts = kDC / 8;   // 16-byte parts per token row
+    for (int c = tid; c < kTok * kXParts; c += NT) {
+      const int tok = c / kXParts;
+      const int part = c % kXParts;
+      const bool ok = t0 + tok < T && part * 8 < dc;
+      const __nv_bfloat16* src = ok ? x + (t0 + tok) * D + d0 + part * 8 : x;
+      cp_async16(xs + tok * kXPitch + part * 16, src, ok ? 16 : 0);
     }
-    // wg[e][d0 + 4*j .. +3] for chunk c = e * (kDC/4) + j (coalesced along d).
-#pragma unroll
-    for (int q = 0; q < kWPerThread; ++q) {
-      const int c = tid + q * NT;
-      const int e = c / (kDC / 4);
-      const int j = c % (kDC / 4);
-      wpre[q] = (c < kWChunks && e < E && 4 * j < dc)
-                    ? __ldg(reinterpret_cast<const float4*>(wg + (int64_t)e * D + d0) + j)
-                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    constexpr int kWParts = kDC / 4;
+    for (int c = tid; c < EMAX * kWParts; c += NT) {
+      const int e = c / kWParts;
+      const int part = c % kWParts;
+      const bool ok = e < E && part * 4 < dc;
+      const float* src = ok ? wg + (int64_t)e * D + d0 + part * 4 : wg;
+      cp_async16(ws + e * kWPitch + part * 16, src, ok ? 16 : 0);
     }
   };
-  load_step(0);
-  for (int d0 = 0; d0 < D; d0 += kDC) {
-    const int dc = min(kDC, D - d0);  // a multiple of 8
-    __syncthreads();
 #pragma unroll
-    for (int q = 0; q < kXPerThread; ++q) {
-      const int c = tid + q * NT;
-      if (c < kXChunks) {
-        const int tok = c % kTok;
-        const int part = c / kTok;
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&xpre[q]);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 f = __bfloat1622float2(h[u]);
-          xs[part * 8 + 2 * u][tok] = f.x;
-          xs[part * 8 + 2 * u + 1][tok] = f.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < kWPerThread; ++q) {
-      const int c = tid + q * NT;
-      if (c < kWChunks) {
-        const int e = c / (kDC / 4);
-        const int j = c % (kDC / 4);
-        ws[4 * j + 0][e] = wpre[q].x;
-        ws[4 * j + 1][e] = wpre[q].y;
-        ws[4 * j + 2][e] = wpre[q].z;
-        ws[4 * j + 3][e] = wpre[q].w;
-      }
-    }
-    __syncthreads();
-    if (d0 + kDC < D) load_step(d0 + kDC);  // in flight during this step's FMAs
+  for (int k = 0; k < kStages - 1; ++k) {
+    if (k < nsteps) issue(k);
+    cp_async_commit();
+  }
+  for (int k = 0; k < nsteps; ++k) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();  // step k has landed for all threads; step k-1's slot is free
+    if (k + kStages - 1 < nsteps) issue(k + kStages - 1);
+    cp_async_commit();
     if (gemm) {
-      float4 xv = *reinterpret_cast<const float4*>(&xs[0][4 * tg]);
-      float4 wv = *reinterpret_cast<const float4*>(&ws[0][4 * eg]);
-#pragma unroll 8
-      for (int dd = 0; dd < dc; ++dd) {
-        // Operands of step dd+1 are loaded before the FMAs of step dd.
-        const int nd = dd + 1 < dc ? dd + 1 : dd;
-        const float4 xn = *reinterpret_cast<const float4*>(&xs[nd][4 * tg]);
-        const float4 wn = *reinterpret_cast<const float4*>(&ws[nd][4 * eg]);
-        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-        const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+      const int dc = min(kDC, D - k * kDC);
+      const uint8_t* xs = x_stage(k % kStages) + tg * kXPitch;
+      const uint8_t* ws = w_stage(k % kStages) + eg * kWPitch;
+#pragma unroll 2
+      for (int d4 = 0; d4 < dc / 4; ++d4) {
+        float xv[4][4], wv[4][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(xs + i * 32 * kXPitch + d4 * 8);
+          xv[i][0] = __uint_as_float(raw.x << 16);
+          xv[i][1] = __uint_as_float(raw.x & 0xffff0000u);
+          xv[i][2] = __uint_as_float(raw.y << 16);
+          xv[i][3] = __uint_as_float(raw.y & 0xffff0000u);
+        }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
-        xv = xn;
-        wv = wn;
+        for (int j = 0; j < 4; ++j) {
+          const float4 q = *reinterpret_cast<const float4*>(ws + j * EG * kWPitch + d4 * 16);
+          wv[j][0] = q.x;
+          wv[j][1] = q.y;
+          wv[j][2] = q.z;
+          wv[j][3] = q.w;
+        }
+#pragma unroll
+        for (int dd = 0; dd < 4; ++dd)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i][dd], wv[j][dd], acc[i][j]);
       }
     }
   }
+  cp_async_wait<0>();
   __syncthreads();  // xs/ws are about to be overwritten by lg
   if (gemm) {
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) lg[4 * tg + i][4 * eg + j] = acc[i][j];
+      for (int j = 0; j < 4; ++j) lg[tg + 32 * i][eg + EG * j] = acc[i][j];
   }
   __syncthreads();
 
