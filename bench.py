@@ -430,7 +430,10 @@ def run_ep(args, world, rank, local):
         import torch.distributed as dist
 
         dist.all_reduce(load)
-        placement = balanced_placement(load.tolist(), world)
+        extra = args.ep_extra_slots
+        if extra < 0:  # replicate only where one expert would bound a rank
+            extra = 0 if world <= 2 else max(2, E // world // 2)
+        placement = balanced_placement(load.tolist(), world, E // world + extra)
         del xc, rc
     m = ExpertParallelSMoE(D, F, E, placement=placement).to(dev)
     m.load_weights(w.wg, w.bg, w.w1, w.b1, w.w2, w.b2)
@@ -505,8 +508,12 @@ def run_ep(args, world, rank, local):
         import torch.distributed as dist
 
         dist.all_reduce(cnt)
-    El = E // world
-    rows_per_rank = cnt.view(world, El).sum(dim=1).tolist()  # router outputs are slots
+    S = m.slots_per_rank
+    nrep = torch.tensor([m.n_rep[e] for e in m.placement], dtype=torch.float64, device=dev)
+    # router outputs are dispatch positions
+    pos = torch.tensor([m.position[e] for e in m.placement], device=dev)
+    share = cnt[pos] / nrep
+    rows_per_rank = share.view(world, S).sum(dim=1).tolist()
     rows_local = rows_per_rank[rank]
     exp_ms = torch.tensor([stages["experts"]], dtype=torch.float64, device=dev)
     if world > 1:
@@ -536,7 +543,8 @@ def run_ep(args, world, rank, local):
                    "parallelism": f"ep{world}",
                    "placement": "contiguous" if placement is None else
                    f"balanced (LPT over the routing counts of a separate {CALIBRATION_TOKENS}-token "
-                   "calibration batch)",
+                   f"calibration batch), {len(placement) // world} slots per rank, "
+                   f"{len(placement) - E} replicas",
                    "exchange": ("none (one rank)" if world == 1 else
                                 "counts: NCCL all_to_all_single; rows: NCCL point-to-point per "
                                 "peer, overlapped with the experts over the rows a rank routes to "
@@ -888,6 +896,9 @@ def main():
                          "cfg5: expert-parallel MoE layer (strong scaling over N)")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="cfg5 expert placement over the ranks")
+    ap.add_argument("--ep-extra-slots", type=int, default=-1,
+                    help="cfg5 replica slots per rank beyond E/N (-1: 0 up to 2 ranks, "
+                         "max(2, E/N/2) above)")
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "all_to_all"],
                     help="cfg5 rows exchange: overlapped point-to-point or plain all_to_all")
     ap.add_argument("--profile", default=None,

@@ -125,7 +125,35 @@ def test_balanced_placement_evens_out_zipf_load():
         ep.balanced_placement([1.0] * 6, 4)
 
 
-def _layer_worker(rank, world, port, splits, overlap, balanced):
+def test_replicated_placement_splits_the_hot_expert():
+    sys.path.insert(0, str(ROOT))
+    import cti_b200.ep as ep
+
+    load = [47.0, 29.0, 13.0, 5.0, 3.0, 1.0, 1.0, 1.0]
+    for world, extra in ((2, 1), (4, 1), (4, 3)):
+        S = len(load) // world + extra
+        pl = ep.balanced_placement(load, world, S)
+        assert len(pl) == world * S and set(pl) == set(range(len(load)))
+        n_rep, rep_idx = ep.replica_tables(pl, len(load))
+        assert sum(n_rep) == world * S and n_rep[0] > 1
+        rank_load = [sum(load[e] / n_rep[e] for e in pl[q * S:(q + 1) * S]) for q in range(world)]
+        plain = ep.balanced_placement(load, world)
+        plain_load = [sum(load[e] for e in plain[q * (len(load) // world):(q + 1) * (len(load) // world)])
+                      for q in range(world)]
+        # LPT bound, and at 4 ranks a real gain over the plain placement
+        # (at 2 ranks the hot expert is already below half of the load).
+        assert max(rank_load) <= sum(load) / world + max(load[e] / n_rep[e] for e in pl) + 1e-9
+        if world > 2:
+            assert max(rank_load) < max(plain_load)
+        # replica shares of a segment cover it exactly, in order
+        for c in (0, 1, 7, 100):
+            n = n_rep[0]
+            parts = [ep.replica_chunk(c, n, i) for i in range(n)]
+            assert sum(sz for _, sz in parts) == c
+            assert all(parts[i][0] + parts[i][1] == parts[i + 1][0] for i in range(n - 1))
+
+
+def _layer_worker(rank, world, port, splits, overlap, balanced, extra=0):
     """ExpertParallelSMoE.forward itself on gloo ranks: its compute stages
     (router, dispatch, expert FFN, combine - CUDA kernels in the product)
     are replaced by the CPU oracle, everything else is the product code."""
@@ -164,7 +192,8 @@ def _layer_worker(rank, world, port, splits, overlap, balanced):
         try:
             placement = None
             if balanced:
-                placement = ep.balanced_placement(torch.softmax(bg, 0).tolist(), world)
+                placement = ep.balanced_placement(torch.softmax(bg, 0).tolist(), world,
+                                                  E // world + extra)
             m = ep.ExpertParallelSMoE(D, F, E, placement=placement)
             m.load_weights(wg, bg, w1, b1, w2, b2)
             m.prepare_for_inference()
@@ -196,10 +225,29 @@ def _layer_worker(rank, world, port, splits, overlap, balanced):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("splits,overlap,balanced", [
-    ([40, 56], True, False), ([40, 56], False, True), ([0, 37], True, True),
-    ([25, 0, 31, 12], True, True), ([25, 9, 31, 12], False, False)])
-def test_expert_parallel_layer_forward_on_gloo(splits, overlap, balanced):
+@pytest.mark.parametrize("splits,overlap,balanced,extra", [
+    ([40, 56], True, False, 0), ([40, 56], True, True, 0), ([0, 37], True, True, 0),
+    ([25, 0, 31, 12], True, True, 0), ([25, 9, 31, 12], False, False, 0),
+    ([40, 56], True, True, 2), ([25, 0, 31, 12], True, True, 1), ([30, 30, 30, 30], True, True, 3)])
+def test_expert_parallel_layer_forward_on_gloo(splits, overlap, balanced, extra):
+    """extra > 0: extra slots per rank, i.e. replicated experts whose rows
+    are split over several ranks."""
     world = len(splits)
-    mp.spawn(_layer_worker, args=(world, _free_port(), splits, overlap, balanced), nprocs=world,
-             join=True)
+    mp.spawn(_layer_worker, args=(world, _free_port(), splits, overlap, balanced, extra),
+             nprocs=world, join=True)
+
+
+def test_dispatch_layout_runs():
+    sys.path.insert(0, str(ROOT))
+    import cti_b200.ep as ep
+
+    # no replicas: one run per rank, dispatch order = the ranks' experts
+    slots, order, runs = ep.dispatch_layout([3, 0, 2, 1], 4, 2)
+    assert sorted(slots[:2]) == [0, 3] and sorted(slots[2:]) == [1, 2]
+    assert order == slots and runs == [[(0, 2)], [(0, 2)]]
+    # expert 0 replicated on both ranks: rank 0 keeps it last among its
+    # primaries, rank 1 holds the second share as an extra replica
+    slots, order, runs = ep.dispatch_layout([0, 1, 2, 0, 3, 4], 5, 2)
+    assert slots[:3] == [1, 2, 0] and order[:3] == [1, 2, 0]
+    assert runs[0] == [(0, 3)]           # 1, 2 and share 0 of expert 0 are adjacent
+    assert len(runs[1]) == 2             # share 1 of expert 0, then experts 3, 4

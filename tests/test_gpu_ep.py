@@ -24,7 +24,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, D, E, F, T, balanced, overlap):
+def _worker(rank, world, port, D, E, F, T, balanced, overlap, extra=0):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -51,8 +51,9 @@ def _worker(rank, world, port, D, E, F, T, balanced, overlap):
         placement = None
         if balanced:
             from cti_b200.ep import balanced_placement
-            placement = balanced_placement(torch.softmax(w.bg, 0).tolist(), world)
-            if world > 1:
+            placement = balanced_placement(torch.softmax(w.bg, 0).tolist(), world,
+                                           E // world + extra)
+            if world > 1 or extra:
                 assert placement != list(range(E))
         ep = ExpertParallelSMoE(D, F, E, placement=placement).to(dev)
         ep.load_global_state_dict(full.state_dict())
@@ -69,12 +70,15 @@ def _worker(rank, world, port, D, E, F, T, balanced, overlap):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("D,E,F,T,balanced,overlap", [(1024, 64, 4096, 8192, False, False),
-                                                      (1024, 64, 4096, 8192, True, True),
-                                                      (256, 16, 1024, 6000, True, True),
-                                                      (256, 16, 1024, 6000, False, True)])
-def test_expert_parallel_layer_matches_single_gpu(D, E, F, T, balanced, overlap):
+@pytest.mark.parametrize("D,E,F,T,balanced,overlap,extra", [
+    (1024, 64, 4096, 8192, False, False, 0),
+    (1024, 64, 4096, 8192, True, True, 0),
+    (1024, 64, 4096, 8192, True, True, 3),   # replicated experts
+    (256, 16, 1024, 6000, True, True, 0),
+    (256, 16, 1024, 6000, True, True, 2),
+    (256, 16, 1024, 6000, False, True, 0)])
+def test_expert_parallel_layer_matches_single_gpu(D, E, F, T, balanced, overlap, extra):
     world = min(2, torch.cuda.device_count())
     assert world >= 1
-    mp.spawn(_worker, args=(world, _free_port(), D, E, F, T, balanced, overlap), nprocs=world,
-             join=True)
+    mp.spawn(_worker, args=(world, _free_port(), D, E, F, T, balanced, overlap, extra),
+             nprocs=world, join=True)
