@@ -477,17 +477,19 @@ class ExpertParallelSMoE(nn.Module):
         return out
 
     def _forward_overlapped(self, d, counts_h, send, recv, send_h, recv_h, mark):
-        """Shift-ordered pipeline over the peers.  Step s (1 <= s < R) sends
-        to rank me+s and receives from rank me-s, one point-to-point op per
-        non-empty run of slot shares (``dispatch_layout``; a single run per
-        peer without replicas), so every pair of ranks meets in the same step.
-        All row transfers are posted first; the experts then work through
-        the received blocks in step order, and each block's results are
-        posted back to their source as soon as they are computed, so the
-        return of block s overlaps the compute of block s+1.  The rows this
-        rank routed to its own slots need no transfer: half of them are
-        computed while the first blocks arrive, the other half while the
-        last results travel back."""
+        """The exchange around the experts, overlapped with their compute.
+
+        Transfers are point-to-point, one op per non-empty run of slot shares
+        (``dispatch_layout``; a single run per peer without replicas).  All
+        outbound rows go in ONE NCCL group over every peer, so all NVSwitch
+        links carry their share at once; meanwhile the experts compute the
+        first half of the rows this rank routed to its own slots (no transfer
+        needed).  Then the received blocks are computed, and their results go
+        back in two all-peer groups: the first while the second half of the
+        blocks is computed, the second while the other half of the own rows
+        is.  Returned rows land directly in the expert-ordered output buffer.
+        Every rank posts the same groups in the same order, so the ops of
+        each pair of ranks match one to one."""
         R, S, me, D = self.world, self.slots_per_rank, self.rank, self.d_model
         ranges = self._send_ranges(counts_h, send_h)
         blk = [sum(recv_h[q]) if q != me else 0 for q in range(R)]
@@ -496,16 +498,6 @@ class ExpertParallelSMoE(nn.Module):
         y_remote = torch.empty_like(rows)
         y = torch.empty_like(d.xperm)
         recv_counts = recv.view(R, S)
-
-        def post(sends, dst, recvs, src):
-            p2p = []
-            for v in recvs:
-                if v.shape[0] > 0:
-                    p2p.append(dist.P2POp(dist.irecv, v, _global(self.group, src), self.group))
-            for v in sends:
-                if v.shape[0] > 0:
-                    p2p.append(dist.P2POp(dist.isend, v, _global(self.group, dst), self.group))
-            return dist.batch_isend_irecv(p2p) if p2p else []
 
         def run_views(buf, base, sizes, q):
             # one view per run of q's slots: contiguous in buf from `base`
@@ -517,11 +509,24 @@ class ExpertParallelSMoE(nn.Module):
             return [d.xperm[ranges[q][j0][0]:ranges[q][j0][0] + sum(n for _, n in ranges[q][j0:j1])]
                     for j0, j1 in self.runs[q]]
 
-        arrivals = {}
-        for step in range(1, R):
-            dst, src = (me + step) % R, (me - step) % R
-            arrivals[step] = post(send_views(dst), dst, run_views(rows, bo[src], recv_h[src], me),
-                                  src)
+        def post_all(pairs):
+            """One NCCL group over several peers: pairs of (sends, dst, recvs, src)."""
+            p2p = []
+            for sends, dst, recvs, src in pairs:
+                for v in recvs:
+                    if v.shape[0] > 0:
+                        p2p.append(dist.P2POp(dist.irecv, v, _global(self.group, src), self.group))
+                for v in sends:
+                    if v.shape[0] > 0:
+                        p2p.append(dist.P2POp(dist.isend, v, _global(self.group, dst), self.group))
+            return dist.batch_isend_irecv(p2p) if p2p else []
+
+        # All outbound rows in one group: every peer link carries its share at
+        # the same time (NVSwitch gives each pair full bandwidth).
+        steps = list(range(1, R))
+        arrivals = post_all([(send_views((me + s) % R), (me + s) % R,
+                              run_views(rows, bo[(me - s) % R], recv_h[(me - s) % R], me),
+                              (me - s) % R) for s in steps])
         mark("exchange")
         # Own slots: gathered into one block unless they are already one.
         own = ranges[me]
@@ -539,18 +544,24 @@ class ExpertParallelSMoE(nn.Module):
         cut = _balanced_cut(own_sizes)
         o_own = _prefix(own_sizes)
         self._ffn_into(own_rows[:o_own[cut]], own_offs[:cut + 1], own_out[:o_own[cut]])
+        for w in arrivals:
+            w.wait()
+        # Remote blocks; their results go back in two groups, the first while
+        # the second half of the blocks is computed.
         returns = []
-        for step in range(1, R):
-            dst, src = (me + step) % R, (me - step) % R
-            for w in arrivals[step]:
-                w.wait()
-            b = slice(bo[src], bo[src + 1])
-            self._ffn_into(rows[b], received_group_offsets(recv_counts[src:src + 1]),
-                           y_remote[b])
-            returns.append(post(run_views(y_remote, bo[src], recv_h[src], me), src,
-                                [y[ranges[dst][j0][0]:ranges[dst][j0][0] +
-                                   sum(n for _, n in ranges[dst][j0:j1])]
-                                 for j0, j1 in self.runs[dst]], dst))
+        half = (len(steps) + 1) // 2
+        for part in (steps[:half], steps[half:]):
+            for s_ in part:
+                src = (me - s_) % R
+                b = slice(bo[src], bo[src + 1])
+                self._ffn_into(rows[b], received_group_offsets(recv_counts[src:src + 1]),
+                               y_remote[b])
+            returns += post_all([
+                (run_views(y_remote, bo[(me - s_) % R], recv_h[(me - s_) % R], me), (me - s_) % R,
+                 [y[ranges[(me + s_) % R][j0][0]:ranges[(me + s_) % R][j0][0] +
+                    sum(n for _, n in ranges[(me + s_) % R][j0:j1])]
+                  for j0, j1 in self.runs[(me + s_) % R]], (me + s_) % R)
+                for s_ in part])
         self._ffn_into(own_rows[o_own[cut]:], own_offs[cut:] - own_offs[cut],
                        own_out[o_own[cut]:], first_expert=cut)
         if not contiguous_own:
@@ -558,8 +569,7 @@ class ExpertParallelSMoE(nn.Module):
                 if n:
                     y[a:a + n].copy_(own_out[o:o + n])
         mark("experts")
-        for ws in returns:
-            for w in ws:
-                w.wait()
+        for w in returns:
+            w.wait()
         mark("exchange_back")
         return y
