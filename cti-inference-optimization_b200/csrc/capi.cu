@@ -63,6 +63,35 @@ extern "C" int cti_num_sms(int device, int* num_sms) {
   return CTI_OK;
 }
 
+namespace cti {
+namespace {
+
+// The library's bounded wait (mbar_wait) with a caller-given limit, on a
+// barrier whose phase never completes.
+__global__ void selftest_wait_kernel(int32_t* status, int64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(&bar, 0)) {
+    if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > (uint64_t)limit_ns) {
+      raise_status(status, CTI_ERR_TIMEOUT, 0x7f0);
+      return;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace cti
+
+extern "C" int cti_selftest_wait_timeout(int32_t* status, int64_t limit_ns, void* stream) {
+  if (!status || limit_ns < 1000 || limit_ns > 2000000000LL) return CTI_ERR_INVALID_ARG;
+  cti::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_ns);
+  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+}
+
 extern "C" int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail,
                                void* stream) {
   if (!status) return CTI_ERR_INVALID_ARG;

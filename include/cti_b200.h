@@ -59,6 +59,15 @@ int cti_num_sms(int device, int* num_sms);
  * synchronises that stream. */
 int cti_status_read(int32_t* status, int clear, int32_t* code, int32_t* detail, void* stream);
 
+/* Self-test of the failure path (no counterpart in the reference): one
+ * thread waits on a shared-memory mbarrier that nothing ever arrives at,
+ * with the same bounded wait as every kernel of the library but a limit of
+ * limit_ns nanoseconds (1e3 <= limit_ns <= 2e9).  When it runs out the
+ * kernel writes CTI_ERR_TIMEOUT (detail 0x7f0) to `status` and returns
+ * normally; the context stays usable.  Lets a test watch a wait run out
+ * without hanging or faulting the GPU. */
+int cti_selftest_wait_timeout(int32_t* status, int64_t limit_ns, void* stream);
+
 /* ------------------------------------------------------------------------
  * Stage 1 - router.
  * Replaces TopKGate.forward (baseline/infer.py:298-309; online_best/infer.py:
