@@ -615,7 +615,7 @@ def run_e2e(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     bb, uo, T = cfg4_batch(seed=rank)
-    model = build_ctr_model(bb.vocab.tolist())
+    model = build_ctr_model(bb.vocab.tolist(), attention=args.attention)
     init_cfg4_model(model)
     model.to(dev)
     model.rep_encoder.emb.weight = torch.nn.Parameter(
@@ -896,6 +896,9 @@ def main():
                          "cfg5: expert-parallel MoE layer (strong scaling over N)")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="cfg5 expert placement over the ranks")
+    ap.add_argument("--attention", default="cti", choices=["cti", "varlen", "padded"],
+                    help="cfg4 attention: this library's kernel, PyTorch varlen flash "
+                         "attention, or SDPA on padded sequences")
     ap.add_argument("--ep-extra-slots", type=int, default=-1,
                     help="cfg5 replica slots per rank beyond E/N (-1: 0 up to 2 ranks, "
                          "max(2, E/N/2) above)")

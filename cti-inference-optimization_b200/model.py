@@ -21,9 +21,11 @@ the reference's parameter names, so a reference state dict loads as is:
     ``baseline/infer.py:437``; ``predict`` applies the sigmoid
     (``baseline/infer.py:686``).
 
-Attention over the packed sequences calls PyTorch's variable-length flash
-attention (``torch.nn.attention.varlen.varlen_attn``) with a causal window;
-the reference builds a dense [T, T] mask instead (``get_sequence_causal_mask``,
+Attention over the packed sequences runs on this library's varlen causal
+attention kernel (``cti_varlen_attention``, head_dim 32) by default, with
+PyTorch's variable-length flash attention (``varlen``) and SDPA over padded
+sequences (``padded``) as the alternatives the tests compare it with; the
+reference builds a dense [T, T] mask instead (``get_sequence_causal_mask``,
 ``baseline/infer.py:420-427``), which does not fit at T = 278k.  This module
 is the model around the hot path; the hot path itself is the MoE layer and
 the pooling.
@@ -69,7 +71,14 @@ def padded_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return o.transpose(1, 2)[seq, pos]
 
 
-ATTENTION = {"varlen": varlen_causal_attention, "padded": padded_causal_attention}
+def cti_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                         cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
+    """The same on this library's kernel (cti_varlen_attention, head_dim 32)."""
+    return ops.varlen_attention(q, k, v, cu_seqlens, max_seqlen)
+
+
+ATTENTION = {"cti": cti_causal_attention, "varlen": varlen_causal_attention,
+             "padded": padded_causal_attention}
 
 
 class TransformerEncoder(nn.Module):
@@ -82,7 +91,7 @@ class TransformerEncoder(nn.Module):
 
     def __init__(self, d_model: int, n_heads: int, num_layers: int, dim_ff: int,
                  num_experts: int = 8, activation: str = "gelu", renormalize: bool = True,
-                 attention: str = "varlen"):
+                 attention: str = "cti"):
         super().__init__()
         if d_model % n_heads:
             raise ValueError("d_model must be a multiple of n_heads")
@@ -215,7 +224,7 @@ class CTRModel(nn.Module):
 def build_ctr_model(vocab_sizes, emb_dim: int = 64, slot_num: int = 28, d_model: int = 256,
                     n_heads: int = 8, num_layers: int = 8, dim_ff: int = 1024,
                     num_experts: int = 16, head_hidden: int = 128,
-                    attention: str = "varlen") -> CTRModel:
+                    attention: str = "cti") -> CTRModel:
     """The configuration-4 model: per-slot tables, 8 layers of 8 heads x 32,
     16 experts of d_ff 1024, MLP head 256 -> 128 -> 1."""
     rep = RepEncoder(vocab_size=int(sum(vocab_sizes)), emb_dim=emb_dim, padding_idx=0,

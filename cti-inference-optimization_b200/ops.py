@@ -226,3 +226,26 @@ def add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.
         "cti_add_layernorm",
     )
     return (x if residual is None else s), out
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
+    """Causal attention inside packed sequences.  q, k, v [T, H, 32] bf16
+    views whose last two dims are contiguous (any token stride, e.g. the
+    thirds of one qkv projection); cu_seqlens int32 [N+1].  Returns a new
+    contiguous [T, H, 32] bf16 tensor."""
+    T, H, hd = q.shape
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda or t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be a bf16 CUDA tensor")
+        if t.shape != q.shape or t.stride(2) != 1 or t.stride(1) != hd:
+            raise ValueError(f"{name} must be [T, H, head_dim] with contiguous heads")
+    require_cuda(cu_seqlens, "cu_seqlens", torch.int32)
+    out = torch.empty((T, H, hd), dtype=torch.bfloat16, device=q.device)
+    check(
+        lib.cti_varlen_attention(ptr(q), ptr(k), ptr(v), q.stride(0), k.stride(0), v.stride(0),
+                                 ptr(cu_seqlens), cu_seqlens.numel() - 1, int(max_seqlen), H, hd,
+                                 ptr(out), stream_handle(q.device)),
+        "cti_varlen_attention",
+    )
+    return out

@@ -213,6 +213,22 @@ int cti_embbag_sum(const int64_t* values, int64_t n_values, const int64_t* row_o
                    int F, int dim, void* out, int out_dtype, int32_t* status, void* stream);
 
 /* ----------------------------------------------------------------------
+ * Causal attention inside packed variable-length sequences (the CTR model's
+ * per-layer attention: baseline/infer.py:267-276 scaled_dot_product with the
+ * sequence causal mask of :420-427; online_best/infer.py:1132-1202).
+ *   out[t, h, :] = softmax over the keys j of t's sequence with j <= t of
+ *                  q[t,h,:].k[j,h,:] / sqrt(head_dim), applied to v[j,h,:]
+ * q, k, v: bf16 [T][heads][head_dim] views with token strides (elements,
+ * multiples of 8, >= heads*head_dim); cu_seqlens int32 [num_seqs+1] token
+ * offsets; out bf16 [T][heads][head_dim] contiguous.  head_dim 32 only
+ * (CTI_ERR_UNSUPPORTED otherwise); any sequence length up to max_seqlen.
+ * ---------------------------------------------------------------------- */
+int cti_varlen_attention(const void* q_bf16, const void* k_bf16, const void* v_bf16,
+                         int64_t q_stride, int64_t k_stride, int64_t v_stride,
+                         const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int heads,
+                         int head_dim, void* out_bf16, void* stream);
+
+/* ----------------------------------------------------------------------
  * Residual add + LayerNorm of the CTR model around the MoE layer: the
  * pre-LN steps of TransformerEncoder.forward (baseline/infer.py:388-409,
  * `residual + y` then nn.LayerNorm) and the RepEncoder LayerNorm over the

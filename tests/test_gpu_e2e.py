@@ -29,7 +29,7 @@ def _build(name, dev, attention):
     return model, batch, sd
 
 
-@pytest.mark.parametrize("attention", ["varlen", "padded"])
+@pytest.mark.parametrize("attention", ["cti", "varlen", "padded"])
 @pytest.mark.parametrize("name", list(gi.E2E_CASES))
 def test_ctr_model_matches_reference_fixture(cuda_device, attention, name):
     """Configuration init (weight std 0.02): encoder output within max rel
@@ -62,8 +62,10 @@ def test_ctr_model_matches_reference_fixture(cuda_device, attention, name):
 
 
 def test_ctr_model_attention_backends_agree(cuda_device):
-    """varlen flash attention and padded SDPA on a larger packed batch."""
-    from cti_b200.model import padded_causal_attention, varlen_causal_attention
+    """This library's kernel, varlen flash attention and padded SDPA on a
+    larger packed batch."""
+    from cti_b200.model import (cti_causal_attention, padded_causal_attention,
+                                varlen_causal_attention)
 
     g = torch.Generator().manual_seed(3)
     lens = torch.randint(1, 257, (64,), generator=g)
@@ -74,7 +76,9 @@ def test_ctr_model_attention_backends_agree(cuda_device):
     cu = cu.to(cuda_device)
     a = varlen_causal_attention(q, k, v, cu, 256).float()
     b = padded_causal_attention(q, k, v, cu, 256).float()
+    c = cti_causal_attention(q, k, v, cu, 256).float()
     assert max_rel_err(a, b) < 1e-2
+    assert max_rel_err(c, b) < 1e-2
     # one sequence against a plain fp32 softmax
     s0, s1 = int(cu[5]), int(cu[6])
     qs, ks, vs = (t[s0:s1].float().transpose(0, 1) for t in (q, k, v))
