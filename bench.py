@@ -2,7 +2,7 @@
 
 Default workload (every N): configuration 2 - one Top-2 MoE layer, d_model
 256, 16 experts, d_ff 1024, 512 packed samples with lengths U{16..256}
-(T = 69,632 tokens for seed 0), bf16 activations and experts, fp32 router,
+(T = 72,214 tokens for seed 0), bf16 activations and experts, fp32 router,
 Zipf(1.2) expert bias.  A step is one SMoE forward over the whole packed
 batch.  With N GPUs every rank runs its own replica on its own batch (the
 layer does not shard at this size), so scaling is weak.
@@ -17,6 +17,12 @@ roofline  the dominant kernel (the expert FFN GEMM) timed alone with CUDA
 cpu_baseline  the reference's PyTorch CPU expert loop (oracle port of
        baseline/infer.py:280-358, fp32) on a bounded token sample, rank 0,
        N=1 only.
+
+Other workloads (--config): cfg3 the 28-feature embedding-bag pooling
+(GB/s); cfg4 the whole CTR model forward (ms per batch); cfg5 the
+expert-parallel layer (d_model 1024, 64 experts, d_ff 4096, 262,144 tokens
+split over the N ranks: strong scaling).  --profile STAGE runs one stage of
+the cfg2 workload alone for an ncu capture.
 
 --impl reference times that CPU implementation alone on the same workload
 (rank 0 only; other ranks exit without work).

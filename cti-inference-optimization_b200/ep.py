@@ -1,26 +1,30 @@
 """Expert-parallel Top-2 MoE across the ranks of a process group.
 
-The reference is single-GPU (SURVEY: no torch.distributed anywhere); this is
-the new multi-GPU form of the same layer for the large-expert configuration
-(d_model 1024, 64 experts, d_ff 4096): rank r owns experts
-[r*E/R, (r+1)*E/R) and its own slice of the packed tokens.
+The reference runs on one GPU and has no torch.distributed anywhere; this is
+the multi-GPU form of the same layer for the large-expert configuration
+(d_model 1024, 64 experts, d_ff 4096).  Every rank holds its own slice of the
+packed tokens and S expert slots; an expert may hold several slots on
+different ranks (replicas), which splits its rows between them.
 
 Per forward, on every rank:
-  1. route the local tokens with the full fp32 router (stage 1);
-  2. dispatch them into expert order (stage 2).  Experts are contiguous per
-     rank, so expert order is destination-rank order and the dispatched rows
-     form one contiguous segment per destination;
-  3. exchange the per-expert row counts (all_to_all_single of int32 counts),
-     then the rows themselves (all_to_all_single with uneven splits, NCCL
-     over NVLink on GPUs);
-  4. run the local experts over the received rows, grouped as (source rank,
-     local expert) - group g uses local weight g % (E/R);
-  5. send the expert outputs back along the reverse splits;
+  1. route the local tokens with the full fp32 router (stage 1), whose rows
+     are stored in dispatch order (``dispatch_layout``): each rank's experts
+     are consecutive;
+  2. dispatch them into that order (stage 2), so the rows for one
+     destination are a few contiguous runs (one without replicas);
+  3. exchange the per-slot row counts (all_to_all_single; one host read of
+     all counts gives the splits), then the rows, point to point, all peers
+     in one NCCL group;
+  4. run the local experts over the rows this rank routed to itself (while
+     the rows travel) and over the received rows, grouped as (source rank,
+     local slot) - group g uses local slot g % S;
+  5. send the expert outputs back in two all-peer groups that overlap the
+     remaining compute, straight into the expert-ordered output buffer;
   6. combine them with the gates at the source rank (stage 4).
 Gates and token ids never leave their rank.
 
-The exchange helpers below are plain torch.distributed code and run on any
-backend (gloo on CPU in the tests, NCCL on GPUs); the compute steps call the
+The exchange code is plain torch.distributed and runs on any backend (gloo
+on CPU in the tests, NCCL over NVLink on GPUs); the compute steps call the
 sm_100a kernels.
 """
 from __future__ import annotations
