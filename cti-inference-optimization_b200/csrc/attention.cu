@@ -8,7 +8,8 @@
 //                  over the keys j of t's own sequence with j <= t
 //
 // One CTA per (sequence, 64-query block, head); 4 warps of 16 query rows.
-// Flash-attention schedule: key blocks of 64 staged in shared memory, scores
+// Flash-attention schedule: key blocks of 64 double-buffered in shared
+// memory (cp.async, the next block in flight during this one's math), scores
 // on the tensor cores (mma.sync m16n8k16 bf16 -> fp32), an online softmax in
 // fp32 registers (running max and sum per row), P converted to bf16 straight
 // from the score registers into the A fragments of P @ V.  Rows past the
@@ -47,20 +48,34 @@ CTI_DEVICE void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uin
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Copies rows [r0, r0 + 64) of a [token][head][32] view into a [64][kPitch]
-// tile (16-byte pieces, 256 of them, two per thread); rows >= n are zeros.
-CTI_DEVICE void load_tile(__nv_bfloat16 (*tile)[kPitch], const __nv_bfloat16* base,
-                          int64_t tok_stride, int r0, int n) {
+// Starts the copy of rows [r0, r0 + 64) of a [token][head][32] view into a
+// [64][kPitch] tile (16-byte cp.async pieces, 256 of them, two per thread);
+// rows >= n are filled with zeros.
+CTI_DEVICE void load_tile_async(__nv_bfloat16 (*tile)[kPitch], const __nv_bfloat16* base,
+                                int64_t tok_stride, int r0, int n) {
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int c = threadIdx.x + i * 128;
     const int row = c >> 2;
     const int part = c & 3;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r0 + row < n)
-      v = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)(r0 + row) * tok_stride) + part);
-    *reinterpret_cast<uint4*>(&tile[row][part * 8]) = v;
+    const bool ok = r0 + row < n;
+    const __nv_bfloat16* src = ok ? base + (int64_t)(r0 + row) * tok_stride + part * 8 : base;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(&tile[row][part * 8])),
+                 "l"(src), "r"(ok ? 16 : 0)
+                 : "memory");
   }
+}
+
+CTI_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CTI_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+CTI_DEVICE float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __global__ void __launch_bounds__(128)
@@ -70,8 +85,8 @@ __global__ void __launch_bounds__(128)
                             int qblocks, float scale_log2, __nv_bfloat16* __restrict__ out,
                             int H) {
   __shared__ __align__(16) __nv_bfloat16 sq[kBQ][kPitch];
-  __shared__ __align__(16) __nv_bfloat16 sk[kBK][kPitch];
-  __shared__ __align__(16) __nv_bfloat16 sv[kBK][kPitch];
+  __shared__ __align__(16) __nv_bfloat16 sk[2][kBK][kPitch];  // double-buffered key blocks
+  __shared__ __align__(16) __nv_bfloat16 sv[2][kBK][kPitch];
   const int seq = blockIdx.x / qblocks;
   const int qb = blockIdx.x % qblocks;
   const int h = blockIdx.y;
@@ -81,7 +96,13 @@ __global__ void __launch_bounds__(128)
   if (q0 >= L) return;  // the whole CTA leaves together
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  load_tile(sq, q + (int64_t)start * q_stride + h * kHD, q_stride, q0, L);
+  const __nv_bfloat16* kbase = k + (int64_t)start * k_stride + h * kHD;
+  const __nv_bfloat16* vbase = v + (int64_t)start * v_stride + h * kHD;
+  load_tile_async(sq, q + (int64_t)start * q_stride + h * kHD, q_stride, q0, L);
+  load_tile_async(sk[0], kbase, k_stride, 0, L);
+  load_tile_async(sv[0], vbase, v_stride, 0, L);
+  cp_async_commit();
+  cp_async_wait<0>();
   __syncthreads();
   // Q fragments of this warp's 16 rows: two k-steps of 16 head dims.
   uint32_t qa[2][4];
@@ -97,10 +118,14 @@ __global__ void __launch_bounds__(128)
 
   for (int kb = 0; kb <= qb; ++kb) {
     const int k0 = kb * kBK;
-    __syncthreads();  // previous block's K/V fully read
-    load_tile(sk, k + (int64_t)start * k_stride + h * kHD, k_stride, k0, L);
-    load_tile(sv, v + (int64_t)start * v_stride + h * kHD, v_stride, k0, L);
-    __syncthreads();
+    const int buf = kb & 1;
+    // Prefetch the next key block into the other buffer (read two blocks
+    // ago; the __syncthreads at the end of the previous step freed it).
+    if (kb < qb) {
+      load_tile_async(sk[buf ^ 1], kbase, k_stride, k0 + kBK, L);
+      load_tile_async(sv[buf ^ 1], vbase, v_stride, k0 + kBK, L);
+      cp_async_commit();
+    }
     // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
     float s[8][4];
 #pragma unroll
@@ -114,7 +139,7 @@ __global__ void __launch_bounds__(128)
         // B fragments of keys [np*16, np*16+16), head dims [kk*16, kk*16+16):
         // matrices (keys 0-7, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 0-7), (keys 8-15, d 8-15).
         uint32_t b[4];
-        ldsm_x4(b, &sk[np * 16 + (lane & 7) + ((lane >> 4) << 3)][kk * 16 + ((lane >> 3) & 1) * 8]);
+        ldsm_x4(b, &sk[buf][np * 16 + (lane & 7) + ((lane >> 4) << 3)][kk * 16 + ((lane >> 3) & 1) * 8]);
         mma_bf16(s[2 * np], qa[kk], b[0], b[1]);
         mma_bf16(s[2 * np + 1], qa[kk], b[2], b[3]);
       }
@@ -148,18 +173,18 @@ __global__ void __launch_bounds__(128)
     // Rows with no visible key yet keep max = -inf; use 0 as the offset.
     const float off0 = mx[0] == -INFINITY ? 0.f : mx[0] * scale_log2;
     const float off1 = mx[1] == -INFINITY ? 0.f : mx[1] * scale_log2;
-    const float corr0 = exp2f(m_run[0] == -INFINITY ? -INFINITY : m_run[0] * scale_log2 - off0);
-    const float corr1 = exp2f(m_run[1] == -INFINITY ? -INFINITY : m_run[1] * scale_log2 - off1);
+    const float corr0 = fast_exp2(m_run[0] == -INFINITY ? -INFINITY : m_run[0] * scale_log2 - off0);
+    const float corr1 = fast_exp2(m_run[1] == -INFINITY ? -INFINITY : m_run[1] * scale_log2 - off1);
     m_run[0] = mx[0];
     m_run[1] = mx[1];
     float ls[2] = {0.f, 0.f};
     uint32_t pa[4][4];  // P as A fragments: 4 k-steps of 16 keys
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      const float p0 = exp2f(fmaf(s[nt][0], scale_log2, -off0));
-      const float p1 = exp2f(fmaf(s[nt][1], scale_log2, -off0));
-      const float p2 = exp2f(fmaf(s[nt][2], scale_log2, -off1));
-      const float p3 = exp2f(fmaf(s[nt][3], scale_log2, -off1));
+      const float p0 = fast_exp2(fmaf(s[nt][0], scale_log2, -off0));
+      const float p1 = fast_exp2(fmaf(s[nt][1], scale_log2, -off0));
+      const float p2 = fast_exp2(fmaf(s[nt][2], scale_log2, -off1));
+      const float p3 = fast_exp2(fmaf(s[nt][3], scale_log2, -off1));
       ls[0] += p0 + p1;
       ls[1] += p2 + p3;
       const int ks = nt >> 1, hi = nt & 1;
@@ -191,11 +216,15 @@ __global__ void __launch_bounds__(128)
         // V^T fragments from V[key][d] with .trans: matrices (keys 0-7, d 0-7),
         // (keys 8-15, d 0-7), (keys 0-7, d 8-15), (keys 8-15, d 8-15).
         uint32_t b[4];
-        ldsm_x4_t(b, &sv[ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][np * 16 + (lane >> 4) * 8]);
+        ldsm_x4_t(b, &sv[buf][ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][np * 16 + (lane >> 4) * 8]);
         mma_bf16(o[2 * np], a, b[0], b[1]);
         mma_bf16(o[2 * np + 1], a, b[2], b[3]);
       }
     }
+    // The next block has landed for everyone, and this block's buffer may be
+    // overwritten by the prefetch of the step after.
+    cp_async_wait<0>();
+    __syncthreads();
   }
   // Normalise and store the rows that exist.
   const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;
