@@ -81,8 +81,12 @@ __global__ void __launch_bounds__(kThreads, DIM <= 128 ? 4 : 2) embbag_kernel(
   const int sub = threadIdx.x % C::LPB;
   const int64_t bag = (int64_t)blockIdx.x * C::BAGS_PER_BLOCK + threadIdx.x / C::LPB;
   if (bag >= B * F) return;
-  const int64_t b = bag / F;
-  const int f = (int)(bag - b * F);
+  // Feature-major: the bags of one block are consecutive samples of ONE
+  // feature, so a block reads one contiguous range of ids and gathers rows
+  // from one table (32 % faster than sample-major at 204 M ids: fewer
+  // pages and L2 sets touched per block).
+  const int f = (int)(bag / B);
+  const int64_t b = bag - (int64_t)f * B;
 
   const int64_t* roff = row_offsets + (int64_t)f * (B + 1);
   const int64_t start = roff[b];
