@@ -9,9 +9,10 @@ layer does not shard at this size), so scaling is weak.
 
 value  tokens/s of the whole job, inputs resident in HBM, device time from
        CUDA events (max over ranks), L2 flushed between steps.
-e2e    the same through the public API with host buffers: pinned host x ->
-       device, SMoE.forward, output -> pinned host, all inside the timed
-       region.
+e2e    the same through the public API with host buffers
+       (SMoE.forward_host -> cti_moe_layer_forward_host): pinned host x ->
+       device, the layer, output -> pinned host, all inside the timed region;
+       the copies of one token chunk overlap the layer on its neighbours.
 roofline  the dominant kernel (the expert FFN GEMM) timed alone with CUDA
        events: algorithmic FLOPs / mean launch time vs the measured bf16 peak.
 cpu_baseline  the reference's PyTorch CPU expert loop (oracle port of
@@ -348,15 +349,14 @@ def run_ours(args, world, rank, local):
     tokens_all = sum_over_ranks(float(T), world, dev)
     value = tokens_all / (step_ms / 1e3)
 
-    # End to end through the public API with host buffers.
+    # End to end through the public API with host buffers: SMoE.forward_host
+    # (cti_moe_layer_forward_host) copies x in, runs the layer and copies the
+    # output back, chunk by chunk, with the copies overlapping the layer.
     x_h = x.cpu().pin_memory()
     out_h = torch.empty_like(x_h).pin_memory()
-    x_d = torch.empty_like(x)
 
     def e2e_step():
-        x_d.copy_(x_h, non_blocking=True)
-        out, _ = m(x_d.unsqueeze(0))
-        out_h.copy_(out[0], non_blocking=True)
+        m.forward_host(x_h, out_h)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -590,6 +590,9 @@ def cfg4_batch(seed: int = 0, samples: int = CFG4_SAMPLES):
     return bb, uo, T
 
 
+E2E_CHUNKS = 8  # sequence groups of the cfg4 host pipeline
+
+
 def init_cfg4_model(model, seed: int = 0):
     """Random init of the configuration: weights and embedding rows
     ~N(0, 0.02), biases 0, LayerNorms (1, 0); every router bias gets the
@@ -649,17 +652,14 @@ def run_e2e(args, world, rank, local):
     _lib.raise_on_status(dev)
     step_ms = max_over_ranks(statistics.median(times), world, dev)
 
-    # End to end: pinned host ids/offsets -> device, forward, probabilities -> host.
+    # End to end: pinned host ids/offsets -> device, forward, probabilities ->
+    # host, through CTRModel.predict_host: the sequences go in E2E_CHUNKS
+    # groups, each group's copy overlapping the previous group's forward.
     pinned = {k: v.pin_memory() for k, v in host.items()}
-    dev_in = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
     probs_h = torch.empty(T, dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        for k in pinned:
-            dev_in[k].copy_(pinned[k], non_blocking=True)
-        b = dict(dev_in)
-        b["max_seqlen"] = 256
-        probs_h.copy_(model.predict(b), non_blocking=True)
+        model.predict_host(pinned, chunks=E2E_CHUNKS, out=probs_h)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -736,7 +736,7 @@ def run_e2e(args, world, rank, local):
                    "l2": "flushed (256 MiB write) before every timed step",
                    "per_gpu": "one replica"},
         "e2e": {"value": e2e_ms, "unit": "ms/batch", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": T * 4},
+                "d2h_bytes_per_step": T * 4, "chunks": E2E_CHUNKS},
         "roofline": {"bound": "tensor", "kernel": "fused_ffn_kernel<256> (one layer, timed alone)",
                      "achieved": ffn_tflops, "peak": float(peaks["bf16_tflops"]),
                      "unit": "TFLOP/s", "frac": ffn_tflops / float(peaks["bf16_tflops"]),

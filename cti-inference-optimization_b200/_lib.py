@@ -62,6 +62,11 @@ SIGNATURES = {
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _P, _P, _SZ, _P, _P],
     ),
+    "cti_moe_layer_forward_host": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _I64, _P, _SZ, _P,
+         _P, _P, _P],
+    ),
     "cti_embbag_sum": (
         _I,
         [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _P, _I, _P, _P],

@@ -141,3 +141,68 @@ extern "C" int cti_moe_layer_forward(const void* x_bf16, const float* wg, const 
   if (rc) return rc;
   return cti_moe_combine(ws.y, R, ws.perm_inv, ws.gate2, T, D, out_bf16, status, stream);
 }
+
+// The whole layer between pinned host buffers, pipelined over chunks of
+// tokens on three streams:
+//   copy_in:  H2D of x chunk i            -> record ev_in
+//   stream:   wait ev_in; layer on chunk i -> record ev_out
+//   copy_out: wait ev_out; D2H of out chunk i
+// cudaStreamWaitEvent binds to the event's latest record at the time of
+// the call, so three events serve every chunk.  Every token's output
+// depends only on its own row (router, expert rows and combine are
+// per-token), so the result equals one cti_moe_layer_forward over all T.
+extern "C" int cti_moe_layer_forward_host(
+    const void* x_host, void* out_host, void* x_dev, void* out_dev, const float* wg,
+    const float* bg, const void* W1_bf16, const float* b1, const void* W2_bf16, const float* b2,
+    int64_t T, int D, int E, int F, int act, int renorm, int64_t chunk_tokens, void* workspace,
+    size_t workspace_bytes, int32_t* status, void* stream, void* copy_stream_in,
+    void* copy_stream_out) {
+  if (T < 0 || D <= 0 || E < 2 || F <= 0 || chunk_tokens <= 0) return CTI_ERR_INVALID_ARG;
+  if (T == 0) return CTI_OK;
+  if (!x_host || !out_host || !x_dev || !out_dev) return CTI_ERR_INVALID_ARG;
+  const int64_t chunk = chunk_tokens < T ? chunk_tokens : T;
+  if (!workspace || workspace_bytes < cti_moe_layer_workspace_bytes(chunk, D, E, F))
+    return CTI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStream_t s_in = static_cast<cudaStream_t>(copy_stream_in);
+  cudaStream_t s_out = static_cast<cudaStream_t>(copy_stream_out);
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // start, in, out
+  for (auto& e : ev)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      for (auto& d : ev)
+        if (d) cudaEventDestroy(d);
+      return CTI_ERR_CUDA;
+    }
+  int rc = CTI_OK;
+  auto cuda_ok = [&](cudaError_t err) {
+    if (err != cudaSuccess && rc == CTI_OK) rc = CTI_ERR_CUDA;
+    return rc == CTI_OK;
+  };
+  const size_t row_bytes = (size_t)D * 2;
+  // The copies start after everything already enqueued on `stream`.
+  if (cuda_ok(cudaEventRecord(ev[0], s)) && cuda_ok(cudaStreamWaitEvent(s_in, ev[0], 0)))
+    cuda_ok(cudaStreamWaitEvent(s_out, ev[0], 0));
+  for (int64_t t0 = 0; rc == CTI_OK && t0 < T; t0 += chunk) {
+    const int64_t n = (T - t0) < chunk ? (T - t0) : chunk;
+    const size_t off = (size_t)t0 * row_bytes, bytes = (size_t)n * row_bytes;
+    uint8_t* xd = static_cast<uint8_t*>(x_dev) + off;
+    uint8_t* od = static_cast<uint8_t*>(out_dev) + off;
+    if (!cuda_ok(cudaMemcpyAsync(xd, static_cast<const uint8_t*>(x_host) + off, bytes,
+                                 cudaMemcpyHostToDevice, s_in)) ||
+        !cuda_ok(cudaEventRecord(ev[1], s_in)) || !cuda_ok(cudaStreamWaitEvent(s, ev[1], 0)))
+      break;
+    rc = cti_moe_layer_forward(xd, wg, bg, W1_bf16, b1, W2_bf16, b2, n, D, E, F, act, renorm, od,
+                               workspace, workspace_bytes, status, stream);
+    if (rc != CTI_OK) break;
+    if (!cuda_ok(cudaEventRecord(ev[2], s)) || !cuda_ok(cudaStreamWaitEvent(s_out, ev[2], 0)))
+      break;
+    cuda_ok(cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + off, od, bytes,
+                            cudaMemcpyDeviceToHost, s_out));
+  }
+  // `stream` resumes after the last copy back (also on an early error, so
+  // that nothing enqueued later races the copies already in flight).
+  if (cudaEventRecord(ev[2], s_out) == cudaSuccess) cudaStreamWaitEvent(s, ev[2], 0);
+  if (cudaEventRecord(ev[1], s_in) == cudaSuccess) cudaStreamWaitEvent(s, ev[1], 0);
+  for (auto& e : ev) cudaEventDestroy(e);
+  return rc;
+}

@@ -220,6 +220,114 @@ class CTRModel(nn.Module):
         logits, _ = self.forward(batch)
         return torch.sigmoid(logits.float()).reshape(-1)
 
+    @torch.no_grad()
+    def predict_host(self, batch: dict, chunks: int = 8,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+        """``predict`` for a batch in host memory (the reference's flat layout,
+        ``online_best/infer.py:742-779`` moves it to the GPU before the
+        forward): the packed sequences are cut into ``chunks`` groups of
+        about equal token count, and the host->device copy of one group's
+        ids and offsets (a side stream) overlaps the forward of the group
+        before it.  Every sequence is computed independently (pooling and
+        MoE per token, attention inside the sequence), so the chunks give
+        the whole batch's probabilities; only the library GEMMs' choice of
+        kernel may change with the row count, within rounding.
+
+        ``batch``: CPU int64 ``_flat_values``, ``_flat_row_offsets``
+        [slot_num*(T+1)], ``_val_offsets`` [slot_num], ``user_offsets``
+        [N+1] (page-locked for the copies to overlap).  Returns page-locked
+        fp32 probabilities [T] (``out`` if given), valid once the current
+        stream is synchronised."""
+        import numpy as np
+
+        dev = self.linear[0].weight.device
+        F = self.rep_encoder.slot_num
+        vals, ro, vo, uo = (batch[k] for k in ("_flat_values", "_flat_row_offsets",
+                                               "_val_offsets", "user_offsets"))
+        for name, t in (("_flat_values", vals), ("_flat_row_offsets", ro),
+                        ("_val_offsets", vo), ("user_offsets", uo)):
+            if t.is_cuda or t.dtype != torch.int64 or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous CPU int64 tensor")
+        if ro.numel() % F:
+            raise ValueError("_flat_row_offsets length must be a multiple of slot_num")
+        T = ro.numel() // F - 1
+        if int(uo[0]) != 0 or int(uo[-1]) != T:
+            raise ValueError("user_offsets must run from 0 to the token count")
+        if out is None:
+            out = torch.empty(T, dtype=torch.float32, pin_memory=True)
+        if T == 0:
+            return out
+        uo_np = uo.numpy()
+        ro_np = ro.numpy().reshape(F, T + 1)
+        vo_np = vo.numpy()
+        # Cut at sequence starts nearest to equal token shares.
+        cuts = np.searchsorted(uo_np, np.linspace(0, T, max(1, int(chunks)) + 1)[1:-1])
+        seq_bounds = np.unique(np.concatenate([[0], cuts, [uo_np.size - 1]]))
+        groups = []
+        for s0, s1 in zip(seq_bounds[:-1], seq_bounds[1:]):
+            a, b = int(uo_np[s0]), int(uo_np[s1])
+            if b > a:
+                groups.append((int(s0), int(s1), a, b))
+        # Per group: value ranges of each feature, the group's val_offsets and
+        # its rebased sequence offsets; all small, copied to the GPU at once.
+        lo = vo_np[None, :] + ro_np[:, [g[2] for g in groups]].T  # [G, F]
+        hi = vo_np[None, :] + ro_np[:, [g[3] for g in groups]].T
+        lens = hi - lo
+        g_vo = np.zeros_like(lens)
+        g_vo[:, 1:] = np.cumsum(lens, axis=1)[:, :-1]
+        small_h = torch.empty(len(groups) * F + uo_np.size + len(groups), dtype=torch.int64,
+                              pin_memory=True)
+        sm = small_h.numpy()
+        sm[:len(groups) * F] = g_vo.reshape(-1)
+        cu_at = len(groups) * F
+        cu_pos = []
+        for (s0, s1, a, _b) in groups:
+            sm[cu_at:cu_at + s1 - s0 + 1] = uo_np[s0:s1 + 1] - a
+            cu_pos.append(cu_at)
+            cu_at += s1 - s0 + 1
+
+        total_vals = int(lens.sum())
+        need = (total_vals, F * (T + len(groups)), small_h.numel())
+        st = getattr(self, "_host_stage", None)
+        if st is None or st[0].device != dev or any(x.numel() < n for x, n in zip(st, need)):
+            st = tuple(torch.empty(n, dtype=torch.int64, device=dev) for n in need)
+            self._host_stage = st
+        vals_d, ro_d, small_d = st
+        s_in = getattr(self, "_copy_stream", None)
+        if s_in is None or s_in.device != dev:
+            s_in = torch.cuda.Stream(dev)
+            self._copy_stream = s_in
+        s_comp = torch.cuda.current_stream(dev)
+        s_in.wait_stream(s_comp)  # staging buffers are free once earlier work is done
+        with torch.cuda.stream(s_in):
+            small_d[:small_h.numel()].copy_(small_h, non_blocking=True)
+        vp = rp = 0
+        for gi, (s0, s1, a, b) in enumerate(groups):
+            n = b - a
+            v0, r0 = vp, rp
+            with torch.cuda.stream(s_in):
+                for f in range(F):
+                    ln = int(lens[gi, f])
+                    if ln:
+                        vals_d[vp:vp + ln].copy_(vals[int(lo[gi, f]):int(hi[gi, f])],
+                                                 non_blocking=True)
+                    vp += ln
+                    base = f * (T + 1)
+                    ro_d[rp:rp + n + 1].copy_(ro[base + a:base + b + 1], non_blocking=True)
+                    rp += n + 1
+                ready = torch.cuda.Event()
+                ready.record(s_in)
+            s_comp.wait_event(ready)
+            ro_g = ro_d[r0:rp].view(F, n + 1)
+            ro_g.sub_(ro_g[:, :1].clone())
+            cu = small_d[cu_pos[gi]:cu_pos[gi] + s1 - s0 + 1]
+            sub = {"_flat_values": vals_d[v0:vp], "_flat_row_offsets": ro_g.view(-1),
+                   "_val_offsets": small_d[gi * F:(gi + 1) * F], "user_offsets": cu,
+                   "max_seqlen": int((uo_np[s0 + 1:s1 + 1] - uo_np[s0:s1]).max())}
+            logits, _ = self.forward(sub)
+            out[a:b].copy_(torch.sigmoid(logits.float()).reshape(-1), non_blocking=True)
+        return out
+
 
 def build_ctr_model(vocab_sizes, emb_dim: int = 64, slot_num: int = 28, d_model: int = 256,
                     n_heads: int = 8, num_layers: int = 8, dim_ff: int = 1024,

@@ -20,7 +20,9 @@ Differences from the reference, by design:
   (``baseline/infer.py:287``, ``:305-309``).  Top-2 ties go to the lower
   expert id in both modes.
 * The router runs in fp32 over bf16 activations whatever the module dtype.
-* There is no CPU or eager fallback: inputs must be bf16 CUDA tensors.
+* There is no CPU or eager fallback: ``forward`` takes bf16 CUDA tensors;
+  ``forward_host`` takes bf16 host tensors and still computes on the GPU
+  (the copies in and out overlap the layer, chunk by chunk).
 """
 from __future__ import annotations
 
@@ -159,6 +161,62 @@ class SMoE(nn.Module):
                 "cti_moe_layer_forward",
             )
         return out.reshape(B, S, D), None
+
+    @torch.no_grad()
+    def forward_host(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None,
+                     chunk_tokens: int | None = None, device: torch.device | None = None):
+        """``forward`` for activations in host memory: copies x to the GPU,
+        runs the layer and copies the output back, pipelined over chunks of
+        tokens (``cti_moe_layer_forward_host``) so that the two copies and
+        the layer overlap.  x_host [..., D] bf16 on the CPU (page-locked
+        for the overlap); returns ``(out_host, None)`` with out_host a
+        page-locked CPU tensor of the same shape, valid once the current
+        stream of ``device`` is synchronised.  The result equals
+        ``forward`` on the same rows bit for bit."""
+        if x_host.is_cuda or x_host.dtype != torch.bfloat16 or x_host.shape[-1] != self.d_model:
+            raise ValueError("x_host must be a CPU bf16 tensor [..., d_model]")
+        if not x_host.is_contiguous():
+            raise ValueError("x_host must be contiguous")
+        dev = device or self.gate.w_g.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("forward_host needs the module on a CUDA device")
+        dev = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+        self._ensure_ready(dev)
+        D = self.d_model
+        T = x_host.numel() // D
+        if out_host is None:
+            out_host = torch.empty(x_host.shape, dtype=torch.bfloat16, pin_memory=True)
+        elif (out_host.shape != x_host.shape or out_host.dtype != torch.bfloat16
+              or out_host.is_cuda or not out_host.is_contiguous()):
+            raise ValueError("out_host must be a contiguous CPU bf16 tensor shaped like x_host")
+        if T == 0:
+            return out_host, None
+        if chunk_tokens is None:
+            # Eight chunks balance the pipeline fill against the per-chunk
+            # launch cost; small layers run in one piece.
+            chunk_tokens = max(4096, -(-T // 8))
+        chunk = min(int(chunk_tokens), T)
+        stage = getattr(self, "_host_stage", None)
+        if stage is None or stage[0].device != dev or stage[0].numel() < T * D:
+            stage = (torch.empty(T * D, dtype=torch.bfloat16, device=dev),
+                     torch.empty(T * D, dtype=torch.bfloat16, device=dev))
+            self._host_stage = stage
+        streams = getattr(self, "_copy_streams", None)
+        if streams is None or streams[0].device != dev:
+            streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+            self._copy_streams = streams
+        ws = self._get_workspace(chunk, dev)
+        check(
+            lib.cti_moe_layer_forward_host(
+                ptr(x_host), ptr(out_host), ptr(stage[0]), ptr(stage[1]), ptr(self._wg),
+                ptr(self._bg), ptr(self._w1), ptr(self._b1), ptr(self._w2), ptr(self._b2), T, D,
+                self.num_experts, self.dim_ff, _lib.ACTIVATIONS[self.activation],
+                int(self.gate.renormalize), chunk, ptr(ws), ws.numel(), ptr(status_word(dev)),
+                stream_handle(dev), streams[0].cuda_stream, streams[1].cuda_stream,
+            ),
+            "cti_moe_layer_forward_host",
+        )
+        return out_host, None
 
     @torch.no_grad()
     def forward_staged(self, x2: torch.Tensor, fused: bool | None = None):

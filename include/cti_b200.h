@@ -193,6 +193,30 @@ int cti_moe_layer_forward(const void* x_bf16, const float* wg, const float* bg,
                           int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Whole layer between host buffers: the SMoE.forward drop-in
+ * (online_best/infer.py:1910-1954) together with the caller's copy of the
+ * activations to the device and of the output back (online_best/infer.py:
+ * 2513 consumes the output on the host side of the plugin in a host-bound
+ * caller).  Tokens are processed in chunks of chunk_tokens; chunk i's
+ * host->device copy (copy_stream_in), layer (stream) and device->host copy
+ * (copy_stream_out) overlap those of its neighbours.  Each token's output
+ * depends only on its own row, so out_host equals cti_moe_layer_forward over
+ * all T, bit for bit.
+ *   x_host, out_host: [T,D] bf16 host memory (page-locked for the copies to
+ *     run asynchronously); x_dev, out_dev: [T,D] bf16 device staging;
+ *   workspace: cti_moe_layer_workspace_bytes(min(chunk_tokens, T), D, E, F).
+ * The copies start after the work enqueued on `stream` before the call, and
+ * `stream` waits for the last copy back, so synchronising `stream` makes
+ * out_host valid.  The copy streams may be `stream` itself (no overlap).
+ * ---------------------------------------------------------------------- */
+int cti_moe_layer_forward_host(const void* x_host, void* out_host, void* x_dev, void* out_dev,
+                               const float* wg, const float* bg, const void* W1_bf16,
+                               const float* b1, const void* W2_bf16, const float* b2, int64_t T,
+                               int D, int E, int F, int act, int renorm, int64_t chunk_tokens,
+                               void* workspace, size_t workspace_bytes, int32_t* status,
+                               void* stream, void* copy_stream_in, void* copy_stream_out);
+
+/* ------------------------------------------------------------------------
  * Stage 5 - 28-feature embedding-bag sum pooling.
  * Replaces fused_all_slots_embedding_kernel and its launch
  * (online_best/infer.py:793-827, :1029-1059) and the per-slot

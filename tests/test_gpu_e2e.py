@@ -128,3 +128,55 @@ def test_cfg4_shaped_model_matches_oracle(cuda_device):
                                                  num_experts=16, table_row_base=bb.table_row_base,
                                                  vocab=bb.vocab)
     np.testing.assert_allclose(probs.cpu().numpy(), ref.numpy(), rtol=0, atol=1e-3)
+
+
+def test_predict_host_chunks_match_predict(cuda_device):
+    """CTRModel.predict_host (host batch, sequences cut into chunks whose
+    host->device copies overlap the previous chunk's forward) against
+    predict on the device batch and against the oracle: probabilities within
+    1e-3 absolute, for 1, 3 and 7 chunks and a repeated call into the same
+    output.  Zero-length bags and a 1-token sequence are included."""
+    import sys
+    from pathlib import Path
+
+    from cti_b200 import _lib, synth
+    from cti_b200.model import build_ctr_model
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+
+    g = torch.Generator().manual_seed(11)
+    lens = torch.randint(16, 257, (20,), generator=g)
+    lens[4] = 1
+    uo = torch.zeros(lens.numel() + 1, dtype=torch.long)
+    uo[1:] = torch.cumsum(lens, 0)
+    T = int(uo[-1])
+    bb = synth.bag_batch(batch=T, seed=5, vocab_lo=1e3, vocab_hi=2e4)
+    model = build_ctr_model(bb.vocab.tolist(), num_layers=2)
+    bench.init_cfg4_model(model, seed=5)
+    with torch.no_grad():
+        model.rep_encoder.emb.weight.copy_(synth.embedding_table(bb.total_rows, 64, seed=5).float())
+        for name, p in model.named_parameters():
+            if "gate" not in name and "emb" not in name:
+                p.copy_(p.bfloat16().float())
+    sd = {k: v.clone() for k, v in model.state_dict().items()}
+    host = {"_flat_values": bb.values, "_flat_row_offsets": bb.row_offsets,
+            "_val_offsets": bb.val_offsets, "user_offsets": uo}
+    model.to(cuda_device).prepare_for_inference()
+    dev_probs = model.predict({k: v.to(cuda_device) for k, v in host.items()}).cpu().numpy()
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    torch.set_num_threads(8)
+    _, _, ref = e2e_ref.ctr_forward_ref(sd, host, slot_num=28, n_heads=8, num_layers=2,
+                                        num_experts=16, table_row_base=bb.table_row_base,
+                                        vocab=bb.vocab)
+    out = None
+    for chunks in (1, 3, 7, 7):
+        probs = model.predict_host(pinned, chunks=chunks, out=out)
+        torch.cuda.current_stream(cuda_device).synchronize()
+        _lib.raise_on_status(cuda_device)
+        assert probs.shape == (T,) and probs.dtype == torch.float32 and not probs.is_cuda
+        if out is not None:
+            assert probs.data_ptr() == out.data_ptr()
+        np.testing.assert_allclose(probs.numpy(), dev_probs, rtol=0, atol=1e-3)
+        np.testing.assert_allclose(probs.numpy(), ref.numpy(), rtol=0, atol=1e-3)
+        out = probs

@@ -154,3 +154,95 @@ def test_expert_forward_runs_on_the_grouped_gemm(cuda_device):
     _lib.raise_on_status(cuda_device)
     ref = mr.expert_ref(x.float().cpu(), w.w1[2].float(), w.b1[2], w.w2[2].float(), w.b2[2], "gelu")
     assert max_rel_err(y, ref) < 1e-2
+
+
+def _cfg2_module(dev, seed=0):
+    from cti_b200 import synth
+    import cti_b200
+
+    cfg = synth.CFG2
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, seed=seed)
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts)
+    synth.load_moe_module(m, w)
+    m.to(dev).prepare_for_inference()
+    return m
+
+
+@pytest.mark.parametrize("T,chunk,pinned", [
+    (None, None, True),     # the cfg2 batch, default chunking (8 chunks)
+    (None, 5000, True),     # ragged last chunk
+    (9000, 100000, True),   # one chunk larger than T
+    (300, 7, True),         # many tiny chunks
+    (1, None, True),
+    (2000, 512, False),     # pageable host memory: copies serialise, same result
+])
+def test_forward_host_equals_device_forward(cuda_device, T, chunk, pinned):
+    """SMoE.forward_host (cti_moe_layer_forward_host: chunked H2D / layer /
+    D2H on three streams) gives the device forward's output bit for bit:
+    every token's output depends only on its own row."""
+    from cti_b200 import _lib, synth
+
+    m = _cfg2_module(cuda_device)
+    if T is None:
+        T, _ = synth.moe_tokens(synth.CFG2, seed=0)
+    x = synth.moe_activations(T, 256, seed=1)
+    ref = m(x.to(cuda_device).unsqueeze(0))[0][0].cpu()
+    x_h = x.pin_memory() if pinned else x.clone()
+    out_h, aux = m.forward_host(x_h, chunk_tokens=chunk)
+    torch.cuda.current_stream(cuda_device).synchronize()
+    _lib.raise_on_status(cuda_device)
+    assert aux is None and out_h.shape == x.shape and not out_h.is_cuda
+    diff = (out_h.float() - ref.float()).abs().max().item()
+    assert torch.equal(out_h, ref), diff
+
+
+def test_forward_host_reuses_buffers_and_orders_after_prior_work(cuda_device):
+    """Back-to-back calls into the same output buffer, then a device forward
+    of another batch: each result is the one for its own input."""
+    from cti_b200 import _lib, synth
+
+    m = _cfg2_module(cuda_device, seed=2)
+    xs = [synth.moe_activations(20000, 256, seed=s) for s in (5, 6)]
+    refs = [m(x.to(cuda_device).unsqueeze(0))[0][0].cpu() for x in xs]
+    out_h = torch.empty(20000, 256, dtype=torch.bfloat16).pin_memory()
+    for x, ref in zip(xs, refs):
+        m.forward_host(x.pin_memory(), out_h, chunk_tokens=3000)
+        torch.cuda.current_stream(cuda_device).synchronize()
+        assert torch.equal(out_h, ref)
+    _lib.raise_on_status(cuda_device)
+
+
+def test_layer_forward_host_c_abi_single_stream_and_errors(cuda_device):
+    """The C entry point with the copy streams equal to the compute stream,
+    and its argument checks."""
+    from cti_b200 import _lib, synth
+    from cti_b200._lib import lib, ptr, stream_handle, status_word
+
+    m = _cfg2_module(cuda_device, seed=4)
+    T, D = 4000, 256
+    x = synth.moe_activations(T, D, seed=4)
+    ref = m(x.to(cuda_device).unsqueeze(0))[0][0].cpu()
+    x_h = x.pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+    xd = torch.empty(T, D, dtype=torch.bfloat16, device=cuda_device)
+    od = torch.empty_like(xd)
+    chunk = 1024
+    ws = torch.empty(int(lib.cti_moe_layer_workspace_bytes(chunk, D, 16, 1024)), dtype=torch.uint8,
+                     device=cuda_device)
+    s = stream_handle(cuda_device)
+
+    def call(xh=x_h, chunk_tokens=chunk, ws_bytes=None):
+        return lib.cti_moe_layer_forward_host(
+            ptr(xh) if xh is not None else None, ptr(out_h), ptr(xd), ptr(od), ptr(m._wg),
+            ptr(m._bg), ptr(m._w1), ptr(m._b1), ptr(m._w2), ptr(m._b2), T, D, 16, 1024,
+            _lib.ACTIVATIONS["gelu"], 1, chunk_tokens, ptr(ws),
+            ws.numel() if ws_bytes is None else ws_bytes, ptr(status_word(cuda_device)), s, s, s)
+
+    assert call() == _lib.CTI_OK
+    torch.cuda.current_stream(cuda_device).synchronize()
+    _lib.raise_on_status(cuda_device)
+    assert torch.equal(out_h, ref)
+    assert call(chunk_tokens=0) == _lib.CTI_ERR_INVALID_ARG
+    assert call(xh=None) == _lib.CTI_ERR_INVALID_ARG
+    assert call(chunk_tokens=2048) == _lib.CTI_ERR_INVALID_ARG  # workspace sized for 1024
+    assert call(ws_bytes=16) == _lib.CTI_ERR_INVALID_ARG
