@@ -280,4 +280,19 @@ CTI_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
 CTI_DEVICE int warp_id() { return threadIdx.x >> 5; }
 CTI_DEVICE int lane_id() { return threadIdx.x & 31; }
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device
+// (the attribute belongs to the function in each device's context); `done`
+// is the caller's per-kernel bit set of devices already configured.
+template <typename Kernel>
+inline cudaError_t ensure_smem_limit(Kernel kernel, int bytes, uint64_t& done) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done & bit)) return cudaSuccess;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) done |= bit;
+  return err;
+}
+
 }  // namespace cti

@@ -457,13 +457,9 @@ int launch_fused(const void* Xp, const void* W1, const float* b1, const void* W2
       !make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, D, D, 128, kBK) ||
       !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * D, (uint64_t)F, (uint64_t)F, D, kBK))
     return CTI_ERR_INVALID_ARG;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(fused_ffn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)P::SMEM) != cudaSuccess)
-      return CTI_ERR_CUDA;
-    attr_set = true;
-  }
+  static uint64_t configured = 0;
+  if (ensure_smem_limit(fused_ffn_kernel<D>, (int)P::SMEM, configured) != cudaSuccess)
+    return CTI_ERR_CUDA;
   const int sms = device_sm_count();
   if (sms <= 0) return CTI_ERR_CUDA;
   const int64_t max_tiles = (rows_total + kBM - 1) / kBM + G;

@@ -245,13 +245,9 @@ int launch_grouped_gemm(const void* A, const void* W, const float* bias, const i
     return CTI_ERR_INVALID_ARG;
   if (!make_tmap_bf16_2d(&tmB, W, (uint64_t)Gw * N, (uint64_t)K, (uint64_t)K, BN, P::BK))
     return CTI_ERR_INVALID_ARG;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)P::SMEM) != cudaSuccess)
-      return CTI_ERR_CUDA;
-    attr_set = true;
-  }
+  static uint64_t configured = 0;
+  if (ensure_smem_limit(grouped_gemm_kernel<BN>, (int)P::SMEM, configured) != cudaSuccess)
+    return CTI_ERR_CUDA;
   const int sms = device_sm_count();
   if (sms <= 0) return CTI_ERR_CUDA;
   const int64_t max_tiles = ((rows_total + P::BM - 1) / P::BM + G) * (N / BN);

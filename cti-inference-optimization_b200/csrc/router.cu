@@ -274,13 +274,10 @@ cudaError_t launch_router(const __nv_bfloat16* x, const float* wg, const float* 
                           int D, int E, int renorm, int32_t* idx2, float* gate2, int32_t* rank,
                           int32_t* hist, cudaStream_t s) {
   const int64_t blocks = (T + kTok - 1) / kTok;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(router_kernel<EMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)RouterSmem<EMAX>::kBytes) != cudaSuccess)
-      return cudaErrorInvalidValue;
-    attr_set = true;
-  }
+  static uint64_t configured = 0;
+  if (ensure_smem_limit(router_kernel<EMAX>, (int)RouterSmem<EMAX>::kBytes, configured) !=
+      cudaSuccess)
+    return cudaErrorInvalidValue;
   router_kernel<EMAX><<<(unsigned)blocks, router_threads<EMAX>(), RouterSmem<EMAX>::kBytes, s>>>(x, wg, bg, T, D, E, renorm, idx2,
                                                             gate2, rank, hist);
   return cudaGetLastError();
