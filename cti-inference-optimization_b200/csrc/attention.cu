@@ -7,8 +7,11 @@
 //   out[t, h, :] = softmax_j( q[t,h,:] . k[j,h,:] / sqrt(32) ) @ v[j,h,:]
 //                  over the keys j of t's own sequence with j <= t
 //
-// One CTA per (sequence, 64-query block, head); 4 warps of 16 query rows.
-// Flash-attention schedule: key blocks of 64 double-buffered in shared
+// Two kernels with the same arithmetic per row.  Sequences of at most 256
+// tokens (max_seqlen <= 256) take varlen_attention_seq_kernel: one CTA per
+// (sequence, head), the whole sequence staged in shared memory.  Longer
+// ones take varlen_attention_kernel: one CTA per (sequence, 64-query block,
+// head); 4 warps of 16 query rows.  Flash-attention schedule: key blocks of 64 double-buffered in shared
 // memory (cp.async, the next block in flight during this one's math), scores
 // on the tensor cores (mma.sync m16n8k16 bf16 -> fp32), an online softmax in
 // fp32 registers (running max and sum per row), P converted to bf16 straight
