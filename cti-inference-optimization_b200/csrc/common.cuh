@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/cti_b200.h"
 
 #define CTI_DEVICE __device__ __forceinline__
@@ -279,6 +281,41 @@ CTI_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
 
 CTI_DEVICE int warp_id() { return threadIdx.x >> 5; }
 CTI_DEVICE int lane_id() { return threadIdx.x & 31; }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch along the layer's kernel chain (router ->
+// scan -> scatter -> expert FFN -> combine).  A kernel launched with
+// launch_dependent() may be scheduled while the previous kernel on the
+// stream is still running; it must call grid_dependency_wait(), in every
+// CTA and before any early exit, before it reads what earlier kernels wrote.
+// The wait returns once the previous grid has completed and its writes are
+// visible; since that grid waited for its own predecessor in the same way,
+// everything earlier on the stream is complete too.  Without the launch
+// attribute the wait returns at once.
+// ---------------------------------------------------------------------------
+CTI_DEVICE void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next kernel on the stream be scheduled before this one finishes
+// (it still waits for this grid to complete before reading its results).
+CTI_DEVICE void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                    size_t smem_bytes, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` once per device
 // (the attribute belongs to the function in each device's context); `done`

@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
   __shared__ int32_t part[kScanThreads];
   __shared__ int32_t total[CTI_MAX_EXPERTS];
   __shared__ int32_t base[CTI_MAX_EXPERTS + 1];
+  grid_dependents_launch();
+  grid_dependency_wait();  // hist comes from the router
   const int tid = threadIdx.x;
   const int chunks = kScanThreads / E;  // block-chunks per expert
   const int64_t per = (nblk + chunks - 1) / chunks;
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(256) dispatch_scatter_kernel(
     int D, int E, int32_t* __restrict__ perm_inv, int32_t* __restrict__ sorted_token,
     __nv_bfloat16* __restrict__ xperm, int32_t* status) {
   __shared__ int2 pos_s[kRowsPerBlock];
+  grid_dependents_launch();
+  grid_dependency_wait();  // routes from the router, block bases from the scan
   const int64_t t0 = (int64_t)blockIdx.x * kRowsPerBlock;
   const int64_t R = 2 * T;
   if (threadIdx.x < kRowsPerBlock) {
@@ -139,6 +143,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                      int32_t* status) {
   __shared__ int2 pos_s[kRowsPerBlock];
   __shared__ float2 gate_s[kRowsPerBlock];
+  grid_dependency_wait();  // Y from the expert FFN
   const int64_t t0 = (int64_t)blockIdx.x * kRowsPerBlock;
   if (threadIdx.x < kRowsPerBlock) {
     const int64_t t = t0 + threadIdx.x;
@@ -215,13 +220,16 @@ extern "C" int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const i
   if (misaligned(idx2, 8) || misaligned(route_rank, 8) || misaligned(perm_inv, 8))
     return CTI_ERR_INVALID_ARG;
   const int64_t nblk = (T + CTI_ROUTER_BLOCK_TOKENS - 1) / CTI_ROUTER_BLOCK_TOKENS;
-  dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(block_hist, nblk, E, offsets);
-  if (cudaGetLastError() != cudaSuccess) return CTI_ERR_CUDA;
+  if (launch_dependent(dispatch_scan_kernel, dim3(1), dim3(kScanThreads), 0, s, block_hist, nblk,
+                       E, offsets) != cudaSuccess)
+    return CTI_ERR_CUDA;
   const int64_t blocks = (T + kRowsPerBlock - 1) / kRowsPerBlock;
-  dispatch_scatter_kernel<<<(unsigned)blocks, 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(x_bf16), idx2, route_rank, block_hist, T, D, E, perm_inv,
-      sorted_token, static_cast<__nv_bfloat16*>(xperm_bf16), status);
-  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+  return launch_dependent(dispatch_scatter_kernel, dim3((unsigned)blocks), dim3(256), 0, s,
+                          static_cast<const __nv_bfloat16*>(x_bf16), idx2, route_rank,
+                          block_hist, T, D, E, perm_inv, sorted_token,
+                          static_cast<__nv_bfloat16*>(xperm_bf16), status) == cudaSuccess
+             ? CTI_OK
+             : CTI_ERR_CUDA;
 }
 
 extern "C" int cti_moe_combine(const void* Y_bf16, int64_t Y_rows, const int32_t* perm_inv,
@@ -237,8 +245,9 @@ extern "C" int cti_moe_combine(const void* Y_bf16, int64_t Y_rows, const int32_t
     return CTI_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t blocks = (T + kRowsPerBlock - 1) / kRowsPerBlock;
-  combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(Y_bf16),
-                                                  Y_rows, perm_inv, gate2, T, D,
-                                                  static_cast<__nv_bfloat16*>(out_bf16), status);
-  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+  return launch_dependent(combine_kernel, dim3((unsigned)blocks), dim3(256), 0, s,
+                          static_cast<const __nv_bfloat16*>(Y_bf16), Y_rows, perm_inv, gate2, T,
+                          D, static_cast<__nv_bfloat16*>(out_bf16), status) == cudaSuccess
+             ? CTI_OK
+             : CTI_ERR_CUDA;
 }

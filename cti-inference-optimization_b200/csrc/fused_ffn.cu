@@ -161,6 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmW1);
     prefetch_tensormap(&tmW2);
   }
+  grid_dependents_launch();
+  grid_dependency_wait();  // offsets and rows come from the dispatch kernels
   Sched sched;
   sched.init(sched_mem, group_offsets, G, rows_total, kBM, 1, status);
   if (warp == 1) {
@@ -464,10 +466,11 @@ int launch_fused(const void* Xp, const void* W1, const float* b1, const void* W2
   if (sms <= 0) return CTI_ERR_CUDA;
   const int64_t max_tiles = (rows_total + kBM - 1) / kBM + G;
   const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-  fused_ffn_kernel<D><<<grid, kThreads, P::SMEM, s>>>(tmX, tmW1, tmW2, offs, G, Gw, rows_total, F,
-                                                       b1, b2, act,
-                                                       static_cast<__nv_bfloat16*>(Y), status);
-  return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
+  return launch_dependent(fused_ffn_kernel<D>, dim3(grid), dim3(kThreads), P::SMEM, s, tmX, tmW1,
+                          tmW2, offs, G, Gw, rows_total, F, b1, b2, act,
+                          static_cast<__nv_bfloat16*>(Y), status) == cudaSuccess
+             ? CTI_OK
+             : CTI_ERR_CUDA;
 }
 
 }  // namespace

@@ -68,6 +68,9 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
     const float* __restrict__ bg, int64_t T, int D, int E, int renorm,
     int32_t* __restrict__ idx2, float* __restrict__ gate2, int32_t* __restrict__ route_rank,
     int32_t* __restrict__ block_hist) {
+  // The dispatch scan may be scheduled now; it waits for this grid to
+  // complete before it reads the histograms.
+  grid_dependents_launch();
   using SM = RouterSmem<EMAX>;
   constexpr int EG = EMAX / 4;       // expert groups of 4
   constexpr int NG = 32 * EG;        // GEMM threads: 32 token groups x EG expert groups
