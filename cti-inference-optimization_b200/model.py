@@ -32,6 +32,9 @@ the pooling.
 """
 from __future__ import annotations
 
+from typing import NamedTuple
+
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -79,6 +82,51 @@ def cti_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 ATTENTION = {"cti": cti_causal_attention, "varlen": varlen_causal_attention,
              "padded": padded_causal_attention}
+
+
+class SequenceGroups(NamedTuple):
+    """A packed batch cut into groups of whole sequences (plan_sequence_groups)."""
+    groups: list        # (first sequence, end sequence, first token, end token) per group
+    lo: np.ndarray      # [G, F] start of each group's ids of feature f in _flat_values
+    hi: np.ndarray      # [G, F] end of those ids
+    lens: np.ndarray    # [G, F] hi - lo
+    val_offsets: np.ndarray  # [G, F] the group's own _val_offsets (ids laid out f by f)
+    cu: np.ndarray      # the groups' sequence offsets, rebased to 0, concatenated
+    cu_start: np.ndarray  # [G] where each group's offsets start in cu
+
+
+def plan_sequence_groups(user_offsets: torch.Tensor, row_offsets: torch.Tensor,
+                         val_offsets: torch.Tensor, slot_num: int, chunks: int) -> SequenceGroups:
+    """Cuts a batch in the reference's flat layout (``_flat_row_offsets``
+    [slot_num*(T+1)] per-feature offsets, ``_val_offsets`` [slot_num],
+    ``user_offsets`` [N+1] token offsets of the packed sequences) into up to
+    ``chunks`` groups of whole sequences with about equal token counts.  Group
+    g holds tokens [a, b); its ids of feature f are ``_flat_values[lo[g, f]:
+    hi[g, f]]``; laid out feature by feature they form the group's own flat
+    batch, whose row offsets are the slice [a, b] of each feature's offsets
+    minus its first value and whose val_offsets are ``val_offsets[g]``."""
+    F = int(slot_num)
+    uo = user_offsets.numpy()
+    T = row_offsets.numel() // F - 1
+    ro = row_offsets.numpy().reshape(F, T + 1)
+    vo = val_offsets.numpy()
+    cuts = np.searchsorted(uo, np.linspace(0, T, max(1, int(chunks)) + 1)[1:-1])
+    bounds = np.unique(np.concatenate([[0], cuts, [uo.size - 1]]))
+    groups = []
+    for s0, s1 in zip(bounds[:-1], bounds[1:]):
+        a, b = int(uo[s0]), int(uo[s1])
+        if b > a:
+            groups.append((int(s0), int(s1), a, b))
+    lo = vo[None, :] + ro[:, [g[2] for g in groups]].T
+    hi = vo[None, :] + ro[:, [g[3] for g in groups]].T
+    lens = hi - lo
+    g_vo = np.zeros_like(lens)
+    g_vo[:, 1:] = np.cumsum(lens, axis=1)[:, :-1]
+    cu = np.concatenate([uo[s0:s1 + 1] - a for (s0, s1, a, _b) in groups]) if groups else \
+        np.zeros(0, dtype=np.int64)
+    starts = np.cumsum([0] + [s1 - s0 + 1 for (s0, s1, _a, _b) in groups])[:-1]
+    return SequenceGroups(groups, lo, hi, lens, g_vo, cu.astype(np.int64),
+                          np.asarray(starts, dtype=np.int64))
 
 
 class TransformerEncoder(nn.Module):
@@ -238,8 +286,6 @@ class CTRModel(nn.Module):
         [N+1] (page-locked for the copies to overlap).  Returns page-locked
         fp32 probabilities [T] (``out`` if given), valid once the current
         stream is synchronised."""
-        import numpy as np
-
         dev = self.linear[0].weight.device
         F = self.rep_encoder.slot_num
         vals, ro, vo, uo = (batch[k] for k in ("_flat_values", "_flat_row_offsets",
@@ -257,34 +303,16 @@ class CTRModel(nn.Module):
             out = torch.empty(T, dtype=torch.float32, pin_memory=True)
         if T == 0:
             return out
-        uo_np = uo.numpy()
-        ro_np = ro.numpy().reshape(F, T + 1)
-        vo_np = vo.numpy()
-        # Cut at sequence starts nearest to equal token shares.
-        cuts = np.searchsorted(uo_np, np.linspace(0, T, max(1, int(chunks)) + 1)[1:-1])
-        seq_bounds = np.unique(np.concatenate([[0], cuts, [uo_np.size - 1]]))
-        groups = []
-        for s0, s1 in zip(seq_bounds[:-1], seq_bounds[1:]):
-            a, b = int(uo_np[s0]), int(uo_np[s1])
-            if b > a:
-                groups.append((int(s0), int(s1), a, b))
-        # Per group: value ranges of each feature, the group's val_offsets and
-        # its rebased sequence offsets; all small, copied to the GPU at once.
-        lo = vo_np[None, :] + ro_np[:, [g[2] for g in groups]].T  # [G, F]
-        hi = vo_np[None, :] + ro_np[:, [g[3] for g in groups]].T
-        lens = hi - lo
-        g_vo = np.zeros_like(lens)
-        g_vo[:, 1:] = np.cumsum(lens, axis=1)[:, :-1]
-        small_h = torch.empty(len(groups) * F + uo_np.size + len(groups), dtype=torch.int64,
-                              pin_memory=True)
+        plan = plan_sequence_groups(uo, ro, vo, F, chunks)
+        groups, lo, hi, lens = plan.groups, plan.lo, plan.hi, plan.lens
+        # The groups' val_offsets and rebased sequence offsets, copied to the
+        # GPU at once.
+        small_h = torch.empty(len(groups) * F + plan.cu.size, dtype=torch.int64, pin_memory=True)
         sm = small_h.numpy()
-        sm[:len(groups) * F] = g_vo.reshape(-1)
-        cu_at = len(groups) * F
-        cu_pos = []
-        for (s0, s1, a, _b) in groups:
-            sm[cu_at:cu_at + s1 - s0 + 1] = uo_np[s0:s1 + 1] - a
-            cu_pos.append(cu_at)
-            cu_at += s1 - s0 + 1
+        sm[:len(groups) * F] = plan.val_offsets.reshape(-1)
+        sm[len(groups) * F:] = plan.cu
+        cu_pos = [len(groups) * F + int(c) for c in plan.cu_start]
+        uo_np = uo.numpy()
 
         total_vals = int(lens.sum())
         need = (total_vals, F * (T + len(groups)), small_h.numel())

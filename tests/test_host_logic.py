@@ -85,3 +85,45 @@ def test_zipf_ids_are_skewed():
     _, counts = np.unique(ids, return_counts=True)
     counts = np.sort(counts)[::-1]
     assert counts[0] > 20 * np.median(counts)
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 7, 25])
+def test_sequence_groups_rebuild_the_batch(chunks):
+    """CTRModel.predict_host's plan (model.plan_sequence_groups): each group's
+    own flat batch (ids of each feature laid out f by f, row offsets sliced
+    and rebased, the planned val_offsets), pooled by the oracle, gives that
+    group's rows of the whole batch's pooling, bit for bit; the groups cover
+    every token once, in order, and cut only at sequence starts."""
+    from cti_b200.model import plan_sequence_groups
+    from oracle import embbag_ref as er
+
+    F = 28
+    g = torch.Generator().manual_seed(11)
+    lens = torch.randint(16, 257, (20,), generator=g)
+    lens[4] = 1
+    uo = torch.zeros(21, dtype=torch.long)
+    uo[1:] = torch.cumsum(lens, 0)
+    T = int(uo[-1])
+    bb = synth.bag_batch(batch=T, seed=5, vocab_lo=1e3, vocab_hi=2e4)
+    table = synth.embedding_table(bb.total_rows, 64, seed=5).float()
+    full = er.embbag_ref(bb.values, bb.row_offsets, bb.val_offsets, table, bb.table_row_base,
+                         bb.vocab, F)
+    plan = plan_sequence_groups(uo, bb.row_offsets, bb.val_offsets, F, chunks)
+    assert 1 <= len(plan.groups) <= chunks
+    assert plan.groups[0][2] == 0 and plan.groups[-1][3] == T
+    starts = set(uo.tolist())
+    parts = []
+    for gi, (s0, s1, a, b) in enumerate(plan.groups):
+        assert a in starts and b in starts and a < b
+        if gi:
+            assert plan.groups[gi - 1][3] == a and plan.groups[gi - 1][1] == s0
+        n = b - a
+        vals = torch.cat([bb.values[int(plan.lo[gi, f]):int(plan.hi[gi, f])] for f in range(F)])
+        ro = torch.cat([bb.row_offsets[f * (T + 1) + a:f * (T + 1) + b + 1] for f in range(F)])
+        ro = (ro.view(F, n + 1) - ro.view(F, n + 1)[:, :1]).reshape(-1)
+        vo = torch.from_numpy(plan.val_offsets[gi])
+        parts.append(er.embbag_ref(vals, ro, vo, table, bb.table_row_base, bb.vocab, F))
+        cu = plan.cu[plan.cu_start[gi]:plan.cu_start[gi] + s1 - s0 + 1]
+        assert cu[0] == 0 and cu[-1] == n
+        np.testing.assert_array_equal(cu, uo[s0:s1 + 1].numpy() - a)
+    assert torch.equal(torch.cat(parts), full)
