@@ -6,7 +6,8 @@
 // prefix / pack kernels) as a deterministic counting sort:
 //   1. dispatch_scan_kernel: one CTA turns the router's per-block expert
 //      histograms into expert offsets[E+1] and per-block base offsets (an
-//      exclusive prefix over blocks, then over experts).
+//      exclusive prefix over blocks, then over experts, with warp-shuffle
+//      scans).
 //   2. dispatch_scatter_kernel: per block of 32 tokens, one thread per token
 //      computes the sorted position of its two routes (block base + in-block
 //      rank from the router), then the block copies the 32 rows to both
@@ -25,9 +26,23 @@ namespace cti {
 namespace {
 
 constexpr int kScanThreads = 1024;
+constexpr int kScanCache = 16;  // block counts a thread keeps in registers between the passes
+
+CTI_DEVICE int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
+  }
+  return v;
+}
 
 // hist: [nblk, E] per-block expert counts; rewritten in place into
-// per-block base positions.  offsets: [E+1].
+// per-block base positions.  offsets: [E+1].  Thread (e, c) owns expert e
+// over one contiguous chunk of blocks; chunk sums are scanned per expert by
+// one warp each (32 chunks per shuffle round), expert totals by warp 0, and
+// each thread then writes its chunk's running bases.  Chunks of up to 16
+// blocks (nblk <= 16 * 1024 / E) stay in registers between the two passes.
 __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __restrict__ hist,
                                                                     int64_t nblk, int E,
                                                                     int32_t* __restrict__ offsets) {
@@ -37,6 +52,7 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
   grid_dependents_launch();
   grid_dependency_wait();  // hist comes from the router
   const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
   const int chunks = kScanThreads / E;  // block-chunks per expert
   const int64_t per = (nblk + chunks - 1) / chunks;
   const int e = tid % E;
@@ -44,37 +60,67 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
   const bool active = c < chunks;
   const int64_t b_lo = active ? c * per : 0;
   const int64_t b_hi = active ? min(nblk, b_lo + per) : 0;
+  const bool cached = per <= kScanCache;
 
+  int32_t cache[kScanCache];
   int32_t sum = 0;
-  for (int64_t b = b_lo; b < b_hi; ++b) sum += hist[b * E + e];
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < kScanCache; ++i) {
+      const int64_t b = b_lo + i;
+      cache[i] = b < b_hi ? hist[b * E + e] : 0;
+    }
+#pragma unroll
+    for (int i = 0; i < kScanCache; ++i) sum += cache[i];
+  } else {
+    for (int64_t b = b_lo; b < b_hi; ++b) sum += hist[b * E + e];
+  }
   part[tid] = sum;
   __syncthreads();
-  if (tid < E) {
-    int32_t run = 0;
-    for (int cc = 0; cc < chunks; ++cc) {
-      const int32_t v = part[cc * E + tid];
-      part[cc * E + tid] = run;
-      run += v;
+  // Exclusive prefix over the chunks of each expert.
+  for (int ee = warp; ee < E; ee += kScanThreads / 32) {
+    int carry = 0;
+    for (int c0 = 0; c0 < chunks; c0 += 32) {
+      const int cc = c0 + lane;
+      const int v = cc < chunks ? part[cc * E + ee] : 0;
+      const int incl = warp_inclusive_scan(v, lane);
+      if (cc < chunks) part[cc * E + ee] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    total[tid] = run;
+    if (lane == 0) total[ee] = carry;
   }
   __syncthreads();
-  if (tid == 0) {
-    int32_t run = 0;
-    for (int ee = 0; ee < E; ++ee) {
-      base[ee] = run;
-      run += total[ee];
+  // Exclusive prefix over the experts.
+  if (warp == 0) {
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int ee = e0 + lane;
+      const int v = ee < E ? total[ee] : 0;
+      const int incl = warp_inclusive_scan(v, lane);
+      if (ee < E) base[ee] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    base[E] = run;
+    if (lane == 0) base[E] = carry;
   }
   __syncthreads();
   if (tid <= E) offsets[tid] = base[tid];
   if (active) {
     int32_t run = base[e] + part[tid];
-    for (int64_t b = b_lo; b < b_hi; ++b) {
-      const int32_t v = hist[b * E + e];
-      hist[b * E + e] = run;
-      run += v;
+    if (cached) {
+#pragma unroll
+      for (int i = 0; i < kScanCache; ++i) {
+        const int64_t b = b_lo + i;
+        if (b < b_hi) {
+          hist[b * E + e] = run;
+          run += cache[i];
+        }
+      }
+    } else {
+      for (int64_t b = b_lo; b < b_hi; ++b) {
+        const int32_t v = hist[b * E + e];
+        hist[b * E + e] = run;
+        run += v;
+      }
     }
   }
 }
