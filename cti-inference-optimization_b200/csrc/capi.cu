@@ -123,15 +123,21 @@ extern "C" int cti_moe_layer_forward(const void* x_bf16, const float* wg, const 
   if ((reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0) return CTI_ERR_INVALID_ARG;
   LayerWorkspace ws(workspace, T, D, E, F);
   const int64_t R = 2 * T;
+  // The dispatched copy of the rows feeds the fused FFN's TMA loads (measured
+  // faster than the fused kernel's in-kernel row gather,
+  // cti_moe_expert_ffn_fused_gather, which would skip the copy); shapes the
+  // fused kernel does not take run two grouped GEMMs.
+  const bool fused = cti_moe_expert_ffn_fused_supported(D, F, E, R) != 0;
   int rc = cti_moe_router(x_bf16, wg, bg, T, D, E, renorm, ws.idx2, ws.gate2, ws.rank, ws.hist,
                           status, stream);
   if (rc) return rc;
   rc = cti_moe_dispatch(x_bf16, ws.idx2, ws.rank, ws.hist, T, D, E, ws.offsets, ws.perm_inv,
                         ws.sorted_token, ws.xperm, status, stream);
   if (rc) return rc;
-  rc = cti_moe_expert_ffn_fused(ws.xperm, W1_bf16, b1, W2_bf16, b2, ws.offsets, E, E, R, D, F,
-                                act, ws.y, status, stream);
-  if (rc == CTI_ERR_UNSUPPORTED) {
+  if (fused) {
+    rc = cti_moe_expert_ffn_fused(ws.xperm, W1_bf16, b1, W2_bf16, b2, ws.offsets, E, E, R, D, F,
+                                  act, ws.y, status, stream);
+  } else {
     rc = cti_moe_grouped_gemm(ws.xperm, W1_bf16, b1, ws.offsets, E, E, R, F, D, act, ws.hidden,
                               status, stream);
     if (rc) return rc;

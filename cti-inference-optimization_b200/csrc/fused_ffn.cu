@@ -95,14 +95,39 @@ CTI_DEVICE void warp_arrive(uint64_t* bar, int lane) {
   if (lane == 0) mbar_arrive(bar);
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+// Row gather (GATHER = true): instead of TMA loads of the dispatched copy
+// Xp, an extra warp copies each tile's 128 rows straight from the token rows
+// x[sorted_token[row]] with 16-byte cp.async into the same 128-byte-swizzled
+// slabs the TMA would fill (row r of a slab at r*128 B, 16-byte chunk c at
+// chunk c ^ (r % 8)); rows at or past rows_total are zero-filled.  It waits
+// for its own copies, fences them into the async proxy the tensor core reads
+// through, and arrives on x_full.  The dispatch then writes only the
+// permutation, not the 2*T*D permuted rows.
+CTI_DEVICE void gather_cp16(uint8_t* smem_dst, const void* gmem_src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(src_bytes)
+               : "memory");
+}
+
+CTI_DEVICE void gather_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// L2 prefetch of one contiguous row (bytes a multiple of 16, 16-byte aligned).
+CTI_DEVICE void prefetch_row_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <int D, bool GATHER>
+__global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
     fused_ffn_kernel(const __grid_constant__ CUtensorMap tmX,
                      const __grid_constant__ CUtensorMap tmW1,
                      const __grid_constant__ CUtensorMap tmW2,
                      const int32_t* __restrict__ group_offsets, int G, int Gw, int64_t rows_total,
                      int F, const float* __restrict__ b1, const float* __restrict__ b2, int act,
-                     __nv_bfloat16* __restrict__ Y, int32_t* status) {
+                     __nv_bfloat16* __restrict__ Y, int32_t* status,
+                     const __nv_bfloat16* __restrict__ x_rows,
+                     const int32_t* __restrict__ sorted_token, int64_t n_tokens) {
   using P = FF<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -202,16 +227,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         const TileCoord tc = sched.decode(t);
         const int gw = tc.g % Gw;
-        if (!mbar_wait(x_empty, (uint32_t)(it & 1) ^ 1u, status, 0x202, abort_flag)) break;
-        mbar_arrive_expect_tx(x_full, (uint32_t)P::X_BYTES);
-        for (int kb = 0; kb < P::XK; ++kb)
-          tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
-        ++x_issued;
-        // The next tile's rows come from HBM; pull them into L2 now so that
-        // their load at the tile boundary does not stall the tensor core.
-        if (t + (int)gridDim.x < total) {
-          const TileCoord nx = sched.decode(t + (int)gridDim.x);
-          for (int kb = 0; kb < P::XK; ++kb) tma_prefetch_l2_2d(&tmX, kb * kBK, nx.row0);
+        if (!GATHER) {
+          if (!mbar_wait(x_empty, (uint32_t)(it & 1) ^ 1u, status, 0x202, abort_flag)) break;
+          mbar_arrive_expect_tx(x_full, (uint32_t)P::X_BYTES);
+          for (int kb = 0; kb < P::XK; ++kb)
+            tma_load_2d(sx + kb * kSlab, &tmX, x_full, kb * kBK, tc.row0);
+          ++x_issued;
+          // The next tile's rows come from HBM; pull them into L2 now so that
+          // their load at the tile boundary does not stall the tensor core.
+          if (t + (int)gridDim.x < total) {
+            const TileCoord nx = sched.decode(t + (int)gridDim.x);
+            for (int kb = 0; kb < P::XK; ++kb) tma_prefetch_l2_2d(&tmX, kb * kBK, nx.row0);
+          }
         }
         for (int s = 0; s < nch + kLag && ok; ++s) {
           if (s < nch) {  // W1 rows [s*128, +128): k-slabs [128 x 64], W1H per half
@@ -337,6 +364,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(drain, 0, status, 0x20b, nullptr);
       }
     }
+  } else if (GATHER && warp == kThreads / 32) {
+    // ------------------------------------------------------------ row gather
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(x_empty, (uint32_t)(it & 1) ^ 1u, status, 0x211, abort_flag);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      const TileCoord tc = sched.decode(t);
+#pragma unroll
+      for (int rr = 0; rr < kBM / 32; ++rr) {
+        const int r = lane + 32 * rr;
+        const int64_t row = (int64_t)tc.row0 + r;
+        int64_t tok = -1;
+        if (row < rows_total) {
+          tok = sorted_token[row];
+          if (tok < 0 || tok >= n_tokens) {
+            raise_status(status, CTI_ERR_BOUNDS, (int32_t)row);
+            tok = -1;
+          }
+        }
+        const uint8_t* src =
+            reinterpret_cast<const uint8_t*>(x_rows + (tok >= 0 ? tok : 0) * (int64_t)D);
+        const int bytes = tok >= 0 ? 16 : 0;
+        uint8_t* dst_row = sx + r * 128;
+#pragma unroll
+        for (int kb = 0; kb < P::XK; ++kb)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            gather_cp16(dst_row + kb * kSlab + ((c ^ (r & 7)) << 4), src + kb * 128 + c * 16,
+                        bytes);
+      }
+      // The next tile's rows into L2 while this tile's copies land.
+      if (t + (int)gridDim.x < total) {
+        const TileCoord nx = sched.decode(t + (int)gridDim.x);
+#pragma unroll
+        for (int rr = 0; rr < kBM / 32; ++rr) {
+          const int64_t row = (int64_t)nx.row0 + lane + 32 * rr;
+          if (row < rows_total) {
+            const int64_t tok = sorted_token[row];
+            if (tok >= 0 && tok < n_tokens) prefetch_row_l2(x_rows + tok * D, (uint32_t)(D * 2));
+          }
+        }
+      }
+      gather_wait_all();
+      fence_proxy_async_smem();
+      warp_arrive(x_full, lane);
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     // 16 warps: four per TMEM lane quadrant q; warp group `sub` owns chunk
@@ -449,26 +523,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D>
+// Xp: the dispatched rows (TMA path), or nullptr with x_rows / sorted_token
+// (row gather).
+template <int D, bool GATHER>
 int launch_fused(const void* Xp, const void* W1, const float* b1, const void* W2, const float* b2,
                  const int32_t* offs, int G, int Gw, int64_t rows_total, int F, int act, void* Y,
-                 int32_t* status, cudaStream_t s) {
+                 int32_t* status, cudaStream_t s, const void* x_rows = nullptr,
+                 const int32_t* sorted_token = nullptr, int64_t n_tokens = 0) {
   using P = FF<D>;
   CUtensorMap tmX, tmW1, tmW2;
-  if (!make_tmap_bf16_2d(&tmX, Xp, (uint64_t)rows_total, D, D, kBM, kBK) ||
-      !make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, D, D, 128, kBK) ||
+  if (!make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, D, D, 128, kBK) ||
       !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * D, (uint64_t)F, (uint64_t)F, D, kBK))
     return CTI_ERR_INVALID_ARG;
+  if (GATHER) {
+    tmX = tmW1;  // not read in gather mode
+  } else if (!make_tmap_bf16_2d(&tmX, Xp, (uint64_t)rows_total, D, D, kBM, kBK)) {
+    return CTI_ERR_INVALID_ARG;
+  }
   static uint64_t configured = 0;
-  if (ensure_smem_limit(fused_ffn_kernel<D>, (int)P::SMEM, configured) != cudaSuccess)
+  if (ensure_smem_limit(fused_ffn_kernel<D, GATHER>, (int)P::SMEM, configured) != cudaSuccess)
     return CTI_ERR_CUDA;
   const int sms = device_sm_count();
   if (sms <= 0) return CTI_ERR_CUDA;
   const int64_t max_tiles = (rows_total + kBM - 1) / kBM + G;
   const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-  return launch_dependent(fused_ffn_kernel<D>, dim3(grid), dim3(kThreads), P::SMEM, s, tmX, tmW1,
-                          tmW2, offs, G, Gw, rows_total, F, b1, b2, act,
-                          static_cast<__nv_bfloat16*>(Y), status) == cudaSuccess
+  return launch_dependent(fused_ffn_kernel<D, GATHER>, dim3(grid),
+                          dim3(GATHER ? kThreads + 32 : kThreads), P::SMEM, s, tmX, tmW1, tmW2,
+                          offs, G, Gw, rows_total, F, b1, b2, act,
+                          static_cast<__nv_bfloat16*>(Y), status,
+                          static_cast<const __nv_bfloat16*>(x_rows), sorted_token,
+                          n_tokens) == cudaSuccess
              ? CTI_OK
              : CTI_ERR_CUDA;
 }
@@ -495,8 +579,44 @@ extern "C" int cti_moe_expert_ffn_fused(const void* Xp_bf16, const void* W1_bf16
     return CTI_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (D == 256)
-    return launch_fused<256>(Xp_bf16, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw, rows_total,
-                             F, act, Y_bf16, status, s);
-  return launch_fused<128>(Xp_bf16, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw, rows_total, F,
-                           act, Y_bf16, status, s);
+    return launch_fused<256, false>(Xp_bf16, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw,
+                                    rows_total, F, act, Y_bf16, status, s);
+  return launch_fused<128, false>(Xp_bf16, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw,
+                                  rows_total, F, act, Y_bf16, status, s);
+}
+
+extern "C" int cti_moe_expert_ffn_fused_supported(int D, int F, int G, int64_t rows_total) {
+  using namespace cti;
+  return (D == 128 || D == 256) && F > 0 && F % kFC == 0 && F <= kMaxF && G >= 1 &&
+                 G <= Sched::kMaxGroups && rows_total >= 0 &&
+                 rows_total < ((int64_t)1 << 31) - 256
+             ? 1
+             : 0;
+}
+
+extern "C" int cti_moe_expert_ffn_fused_gather(const void* x_bf16, int64_t T,
+                                               const int32_t* sorted_token, const void* W1_bf16,
+                                               const float* b1, const void* W2_bf16,
+                                               const float* b2, const int32_t* group_offsets,
+                                               int G, int Gw, int64_t rows_total, int D, int F,
+                                               int act, void* Y_bf16, int32_t* status,
+                                               void* stream) {
+  using namespace cti;
+  if (G < 1 || Gw < 1 || rows_total < 0 || F <= 0 || T < 0) return CTI_ERR_INVALID_ARG;
+  if (act < CTI_ACT_NONE || act > CTI_ACT_GELU) return CTI_ERR_INVALID_ARG;
+  if ((D != 128 && D != 256) || F % kFC != 0 || F > kMaxF || G > Sched::kMaxGroups)
+    return CTI_ERR_UNSUPPORTED;
+  if (rows_total >= ((int64_t)1 << 31) - 256) return CTI_ERR_UNSUPPORTED;
+  if (!W1_bf16 || !W2_bf16 || !b1 || !b2 || !group_offsets || !Y_bf16) return CTI_ERR_INVALID_ARG;
+  if (rows_total == 0) return CTI_OK;
+  if (!x_bf16 || !sorted_token || T == 0) return CTI_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) || (reinterpret_cast<uintptr_t>(Y_bf16) & 15) ||
+      (reinterpret_cast<uintptr_t>(b1) & 15) || (reinterpret_cast<uintptr_t>(b2) & 15))
+    return CTI_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 256)
+    return launch_fused<256, true>(nullptr, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw,
+                                   rows_total, F, act, Y_bf16, status, s, x_bf16, sorted_token, T);
+  return launch_fused<128, true>(nullptr, W1_bf16, b1, W2_bf16, b2, group_offsets, G, Gw,
+                                 rows_total, F, act, Y_bf16, status, s, x_bf16, sorted_token, T);
 }

@@ -143,6 +143,44 @@ def expert_ffn_fused(
     return out
 
 
+def expert_ffn_fused_gather(
+    x: torch.Tensor,
+    sorted_token: torch.Tensor,
+    w1: torch.Tensor,
+    b1: torch.Tensor,
+    w2: torch.Tensor,
+    b2: torch.Tensor,
+    group_offsets: torch.Tensor,
+    act: str = "gelu",
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Stage 3, fused, rows gathered in the kernel: row r is x[sorted_token[r]]
+    (no dispatched copy of the rows).  Equals expert_ffn_fused on the
+    dispatched rows bit for bit."""
+    require_cuda(x, "x", torch.bfloat16)
+    require_cuda(sorted_token, "sorted_token", torch.int32)
+    require_cuda(w1, "W1", torch.bfloat16)
+    require_cuda(w2, "W2", torch.bfloat16)
+    require_cuda(b1, "b1", torch.float32)
+    require_cuda(b2, "b2", torch.float32)
+    T, D = x.shape
+    rows = sorted_token.numel()
+    Gw, F, _ = w1.shape
+    G = group_offsets.numel() - 1
+    dev = x.device
+    if out is None:
+        out = torch.empty((rows, D), dtype=torch.bfloat16, device=dev)
+    check(
+        lib.cti_moe_expert_ffn_fused_gather(
+            ptr(x), T, ptr(sorted_token), ptr(w1), ptr(b1), ptr(w2), ptr(b2), ptr(group_offsets),
+            G, Gw, rows, D, F, _lib.ACTIVATIONS[act], ptr(out), ptr(status_word(dev)),
+            stream_handle(dev),
+        ),
+        "cti_moe_expert_ffn_fused_gather",
+    )
+    return out
+
+
 def combine(y: torch.Tensor, perm_inv: torch.Tensor, gate2: torch.Tensor,
             out: torch.Tensor | None = None) -> torch.Tensor:
     """Stage 4: out[t] = g0*Y[perm_inv[t,0]] + g1*Y[perm_inv[t,1]] (fp32 math, bf16 out)."""

@@ -104,7 +104,8 @@ size_t cti_moe_dispatch_workspace_bytes(int64_t T, int E);
  * places every route r=(t,k) at position pos = offsets[e] + (number of
  * earlier routes to e in token order): perm_inv[t,k] = pos,
  * sorted_token[pos] = t, xperm[pos,:] = x[t,:].  Deterministic.
- * xperm may be NULL (positions only; used by expert parallelism).
+ * xperm may be NULL (positions only): expert parallelism moves rows
+ * itself, and cti_moe_expert_ffn_fused_gather reads them from x.
  * ---------------------------------------------------------------------- */
 int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const int32_t* route_rank,
                      int32_t* block_hist, int64_t T, int D, int E, int32_t* offsets,
@@ -165,6 +166,25 @@ int cti_moe_expert_ffn_fused(const void* Xp_bf16, const void* W1_bf16, const flo
                              const void* W2_bf16, const float* b2, const int32_t* group_offsets,
                              int G, int Gw, int64_t rows_total, int D, int F, int act,
                              void* Y_bf16, int32_t* status, void* stream);
+
+/* The same with the rows gathered in the kernel: row r of the expert-sorted
+ * order is x[sorted_token[r], :] (x [T, D] bf16, sorted_token [rows_total]
+ * from cti_moe_dispatch), so the dispatch need not write Xp (pass
+ * xperm_bf16 = NULL there).  This replaces the fc1 kernel's row gather of
+ * online_best/infer.py:1329-1333 as well.  Results equal
+ * cti_moe_expert_ffn_fused on the dispatched rows, bit for bit.  One extra
+ * warp copies the rows (16-byte cp.async); at the cfg2 shape the layer built
+ * on it took 0.279 ms against 0.248 ms with the dispatched copy and TMA, so
+ * cti_moe_layer_forward keeps the copy. */
+int cti_moe_expert_ffn_fused_gather(const void* x_bf16, int64_t T, const int32_t* sorted_token,
+                                    const void* W1_bf16, const float* b1, const void* W2_bf16,
+                                    const float* b2, const int32_t* group_offsets, int G, int Gw,
+                                    int64_t rows_total, int D, int F, int act, void* Y_bf16,
+                                    int32_t* status, void* stream);
+
+/* 1 if the fused kernels take this shape (D in {128, 256}, F % 128 == 0,
+ * F <= 1024, G <= 256 groups, rows_total < 2^31 - 256), else 0. */
+int cti_moe_expert_ffn_fused_supported(int D, int F, int G, int64_t rows_total);
 
 /* ------------------------------------------------------------------------
  * Stage 4 - gate-weighted combine.

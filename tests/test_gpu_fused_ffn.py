@@ -107,3 +107,55 @@ def test_gelu_epilogue_accuracy(cuda_device):
     assert (err[inner] <= exact[inner].abs() * 2.0 ** -7 + 1e-30).all(), err[inner].max()
     assert (err <= 2e-6 + exact.abs() * 2.0 ** -7).all(), err.max()
     assert torch.equal(out[:, :64].cpu(), out[:, 64:].cpu())
+
+
+@pytest.mark.parametrize("D,Fd,T,E,act", [
+    (256, 1024, 72214, 16, "gelu"),   # the cfg2 layer's shape
+    (128, 512, 3001, 8, "gelu"),
+    (256, 512, 5, 4, "relu"),         # partial tiles only
+    (128, 256, 900, 3, "none"),
+])
+def test_fused_ffn_row_gather_equals_dispatched_rows(cuda_device, D, Fd, T, E, act):
+    """cti_moe_expert_ffn_fused_gather (rows x[sorted_token[r]] copied by the
+    kernel's gather warp into the swizzled tile) against the TMA path on the
+    dispatched copy of the same rows: bit for bit."""
+    from cti_b200 import _lib, ops, synth
+
+    g = torch.Generator().manual_seed(T)
+    x = (torch.randn(T, D, generator=g)).bfloat16().to(cuda_device)
+    wg = (torch.randn(E, D, generator=g) * 0.05).to(cuda_device)
+    bg = torch.zeros(E).to(cuda_device)
+    w1 = (torch.randn(E, Fd, D, generator=g) * 0.02).bfloat16().to(cuda_device)
+    b1 = (torch.randn(E, Fd, generator=g) * 0.02).to(cuda_device)
+    w2 = (torch.randn(E, D, Fd, generator=g) * 0.02).bfloat16().to(cuda_device)
+    b2 = (torch.randn(E, D, generator=g) * 0.02).to(cuda_device)
+    r = ops.router(x, wg, bg)
+    d = ops.dispatch(x, r, E)
+    y_tma = ops.expert_ffn_fused(d.xperm, w1, b1, w2, b2, d.offsets, act=act)
+    y_gather = ops.expert_ffn_fused_gather(x, d.sorted_token, w1, b1, w2, b2, d.offsets, act=act)
+    _lib.raise_on_status(cuda_device)
+    assert torch.equal(y_gather, y_tma), (y_gather.float() - y_tma.float()).abs().max().item()
+
+
+def test_layer_matches_staged_fused_and_support_query(cuda_device):
+    """SMoE.forward (cti_moe_layer_forward) equals the staged path (dispatched
+    copy, TMA fused FFN, combine) bit for bit at the cfg2 shape, and the
+    fused-shape query answers for the layer's shapes."""
+    from cti_b200 import _lib, synth
+    from cti_b200._lib import lib
+    import cti_b200
+
+    assert lib.cti_moe_expert_ffn_fused_supported(256, 1024, 16, 144428) == 1
+    assert lib.cti_moe_expert_ffn_fused_supported(1024, 4096, 64, 1000) == 0
+    assert lib.cti_moe_expert_ffn_fused_supported(256, 1000, 16, 1000) == 0
+    cfg = synth.CFG2
+    T, _ = synth.moe_tokens(cfg, seed=0)
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, seed=7)
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device).prepare_for_inference()
+    x = synth.moe_activations(T, cfg.d_model, seed=7).to(cuda_device)
+    out = m(x.unsqueeze(0))[0][0]
+    staged = m.forward_staged(x, fused=True)["out"]
+    _lib.raise_on_status(cuda_device)
+    assert torch.equal(out, staged)
