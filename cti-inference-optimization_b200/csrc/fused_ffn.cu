@@ -22,8 +22,9 @@
 // turns chunk c into H(c), the tensor core runs GEMM2(c-1) and GEMM1(c+1).
 // After the last chunk, acc2 + b2 is written to Y as bf16.
 //
-// Roles (576 threads): warp 0 TMA producer (X tile once per tile; W1 and W2
-// chunks through two rings of whole-chunk slots), warp 1 TMEM owner and MMA issuer
+// Roles (576 threads; 608 with the row gather below): warp 0 TMA producer
+// (X tile once per tile unless warp 18 gathers it; W1 and W2 chunks through
+// two rings of whole-chunk slots), warp 1 TMEM owner and MMA issuer
 // (tcgen05.mma M=128, K=16, bf16 -> fp32; N=128 for GEMM1, N=D for GEMM2),
 // warps 2-17 epilogue (four warps per TMEM lane quadrant, each owning 32 of
 // a chunk's 128 columns and a quarter of the output columns; the expert's
