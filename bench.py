@@ -830,6 +830,8 @@ def run_profile_workload(args):
         "dispatch": lambda: ops.dispatch(x, ops.router(x, m._wg, m._bg), m.num_experts),
         "ffn_fused": lambda: ops.expert_ffn_fused(d.xperm, m._w1, m._b1, m._w2, m._b2,
                                                   d.offsets, out=y),
+        "ffn_gather": lambda: ops.expert_ffn_fused_gather(x, d.sorted_token, m._w1, m._b1, m._w2,
+                                                          m._b2, d.offsets, out=y),
         "ffn_fc1": lambda: ops.grouped_gemm(d.xperm, m._w1, m._b1, d.offsets, act="gelu"),
         "combine": lambda: ops.combine(y, d.perm_inv, r.gate2),
         "layer": lambda: m(x.unsqueeze(0)),
@@ -935,8 +937,8 @@ def main():
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "all_to_all"],
                     help="cfg5 rows exchange: overlapped point-to-point or plain all_to_all")
     ap.add_argument("--profile", default=None,
-                    choices=["router", "dispatch", "ffn_fused", "ffn_fc1", "combine", "layer",
-                             "embbag"],
+                    choices=["router", "dispatch", "ffn_fused", "ffn_gather", "ffn_fc1", "combine",
+                             "layer", "embbag"],
                     help="run one stage of the configuration-2 workload for an ncu capture")
     args = ap.parse_args()
     if args.profile:
