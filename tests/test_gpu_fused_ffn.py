@@ -119,7 +119,7 @@ def test_fused_ffn_row_gather_equals_dispatched_rows(cuda_device, D, Fd, T, E, a
     """cti_moe_expert_ffn_fused_gather (rows x[sorted_token[r]] copied by the
     kernel's gather warp into the swizzled tile) against the TMA path on the
     dispatched copy of the same rows: bit for bit."""
-    from cti_b200 import _lib, ops, synth
+    from cti_b200 import _lib, ops
 
     g = torch.Generator().manual_seed(T)
     x = (torch.randn(T, D, generator=g)).bfloat16().to(cuda_device)
