@@ -64,6 +64,33 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def stage_bandwidths(stages_ms: dict, T: int, D: int, E: int, hbm_gbs: float) -> dict:
+    """Algorithmic HBM bytes of the layer's memory-bound stages (bf16 rows,
+    int32 indices, fp32 gates, 128-token router blocks) over their stage
+    times: GB/s and the fraction of the measured copy bandwidth.  Stages
+    missing from `stages_ms` are left out."""
+    R = 2 * T
+    nblk = -(-T // 128)
+    row = 2 * D
+    nbytes = {
+        # x read; idx2, gate2 and route ranks written; per-block histograms written
+        "router": T * row + T * 2 * (4 + 4 + 4) + nblk * E * 4,
+        # scan: histograms read and rewritten; scatter: routes and ranks read, x read
+        # once and written to both sorted slots, perm_inv and sorted_token written
+        "dispatch": 2 * nblk * E * 4 + T * 2 * (4 + 4) + T * row + R * row + T * 2 * 4 + R * 4,
+        # both expert rows of every token read, the output row written; perm_inv, gates read
+        "combine": R * row + T * row + T * 2 * (4 + 4),
+    }
+    out = {}
+    for name, b in nbytes.items():
+        ms = stages_ms.get(name)
+        if not ms:
+            continue
+        gbs = b / (ms / 1e3) / 1e9
+        out[name] = {"bytes": b, "gbs": gbs, "frac_of_hbm": gbs / hbm_gbs}
+    return out
+
+
 # ---------------------------------------------------------------------------
 # clocks during the timed region
 # ---------------------------------------------------------------------------
@@ -402,6 +429,8 @@ def run_ours(args, world, rank, local):
                      "flops_per_launch": dom_flops, "traffic": None},
         "layer_roofline_frac": (2 * gemm_flops * world / (step_ms / 1e3) / 1e12 / world) / peak,
         "stages_ms": stages,
+        "stages_hbm": stage_bandwidths(stages, T, cfg.d_model, cfg.num_experts,
+                                       float(peaks["hbm_gbs"])),
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,

@@ -38,3 +38,23 @@ def test_reference_arm_prints_one_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_stage_bandwidths_algorithmic_bytes():
+    """The cfg2 line's `stages_hbm`: algorithmic bytes of router, dispatch
+    and combine at T = 72,214, D = 256, E = 16 (38.7 / 113.3 / 112.1 MB; the
+    dispatch figure includes the scan's pass over the block histograms), over
+    the stage times."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    stages = {"router": 0.030, "dispatch": 0.030, "combine": 0.025, "ffn_fused": 0.18}
+    out = bench.stage_bandwidths(stages, 72214, 256, 16, 6552.6)
+    assert set(out) == {"router", "dispatch", "combine"}
+    assert round(out["router"]["bytes"] / 1e6, 1) == 38.7
+    assert round(out["dispatch"]["bytes"] / 1e6, 1) == 113.3
+    assert round(out["combine"]["bytes"] / 1e6, 1) == 112.1
+    c = out["combine"]
+    assert abs(c["gbs"] - c["bytes"] / 25e-6 / 1e9) < 1e-6
+    assert abs(c["frac_of_hbm"] - c["gbs"] / 6552.6) < 1e-12
+    assert bench.stage_bandwidths({"router": 0.03}, 1000, 128, 8, 6552.6).keys() == {"router"}
