@@ -1,6 +1,7 @@
-// Library-level entry points: identity, device query, status words, and
-// the one-call MoE layer (router -> dispatch -> expert FFN -> combine) that
-// mirrors SMoE.forward (online_best/infer.py:1910-1954) for C callers.
+// Library-level entry points: identity, device query, status words, the
+// one-call MoE layer (router -> dispatch -> expert FFN -> combine) that
+// mirrors SMoE.forward (online_best/infer.py:1910-1954) for C callers, and
+// the same layer between host buffers, pipelined over token chunks.
 #include <cstring>
 
 #include "common.cuh"
