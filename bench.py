@@ -53,7 +53,6 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 L2_FLUSH_BYTES = 256 << 20
 CPU_SAMPLE_TOKENS = 8192
 CALIBRATION_TOKENS = 65536
-CFG4_SAMPLES = 2048
 
 
 def load_peaks():
@@ -196,13 +195,34 @@ def sum_over_ranks(v: float, world: int, dev) -> float:
 # ---------------------------------------------------------------------------
 # CPU baseline (the oracle port of the reference's expert loop)
 # ---------------------------------------------------------------------------
-def cpu_baseline_moe(cfg, seconds: float, sample_tokens: int = CPU_SAMPLE_TOKENS):
-    from cti_b200 import synth
+def load_synth():
+    """The package's synth.py loaded on its own.  Importing it through the
+    package would load libcti_b200.so, which the reference arm must never
+    map: that arm runs only the reference's CPU code path."""
+    import importlib.util
+
+    name = "_cti_b200_synth_standalone"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(
+        name, ROOT / "cti-inference-optimization_b200" / "synth.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def cpu_baseline_moe(cfg, seconds: float, sample_tokens: int | None = CPU_SAMPLE_TOKENS):
+    """The oracle port of the reference's fp32 expert loop
+    (baseline/infer.py:280-358) on all host cores, repeated for about
+    `seconds`, on the first `sample_tokens` tokens of the configuration
+    (all of them when None)."""
     from oracle import moe_ref as mr
 
+    synth = load_synth()
     torch.set_num_threads(os.cpu_count() or 1)
     T, _ = synth.moe_tokens(cfg)
-    S = min(sample_tokens, T)
+    S = T if sample_tokens is None else min(sample_tokens, T)
     w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias)
     x = synth.moe_activations(T, cfg.d_model)[:S].float()
     w1, w2 = w.w1.float(), w.w2.float()
@@ -217,24 +237,26 @@ def cpu_baseline_moe(cfg, seconds: float, sample_tokens: int = CPU_SAMPLE_TOKENS
             if (el >= seconds and n >= 2) or n >= 10000:
                 break
     return {"value": n * S / el, "unit": "tokens/s", "cores": torch.get_num_threads(),
-            "kind": "port",
+            "kind": "port", "config": cfg.name,
             "sample": f"{S} of the {T} {cfg.name} tokens per call, {n} calls "
                       f"({el:.1f} s), fp32, oracle/moe_ref.py (baseline/infer.py:280-358)"}
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's CPU expert loop (oracle port) on rank 0."""
+    """--impl reference: the reference's CPU expert loop (the oracle port of
+    baseline/infer.py:280-358, fp32, all host cores) over the whole
+    configuration-2 batch, on rank 0 only.  It never loads this repository's
+    library: synth.py is loaded on its own and the oracle is plain torch."""
     if rank != 0:
         return
-    from cti_b200 import synth
     from oracle import moe_ref as mr
 
+    synth = load_synth()
     cfg = synth.CFG2
     torch.set_num_threads(os.cpu_count() or 1)
     T, _ = synth.moe_tokens(cfg)
-    S = min(CPU_SAMPLE_TOKENS, T)
     w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias)
-    x = synth.moe_activations(T, cfg.d_model)[:S].float()
+    x = synth.moe_activations(T, cfg.d_model).float()
     w1, w2 = w.w1.float(), w.w2.float()
     times = []
     with torch.no_grad():
@@ -244,34 +266,32 @@ def run_reference(args, world, rank):
             if i >= args.warmup:
                 times.append(time.perf_counter() - t0)
     step = statistics.mean(times)
-    value = S / step
+    value = T / step
     line = {
         "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": value,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(cfg, T, sample=S),
+        "config": workload_config(cfg, T),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{S} of {T} tokens per step (oracle/moe_ref.py, the "
-                                   f"reference's fp32 expert loop)"},
+                         "sample": f"all {T} tokens per step (oracle/moe_ref.py, the "
+                                   f"reference's fp32 expert loop, baseline/infer.py:280-358)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def workload_config(cfg, T, sample=None):
-    c = {"workload": f"{cfg.name}: Top-2 MoE layer, d_model {cfg.d_model}, {cfg.num_experts} "
-                     f"experts, d_ff {cfg.dim_ff}, {cfg.samples} packed samples U{{16..256}}",
-         "tokens": T, "d_model": cfg.d_model, "experts": cfg.num_experts, "d_ff": cfg.dim_ff,
-         "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
-         "l2": "flushed (256 MiB write) before every timed step",
-         "host": "enqueue hidden behind a device-side wait before each timed step (value); "
-                 "included in e2e", "per_gpu": "one replica"}
-    if sample is not None:
-        c["cpu_sample_tokens"] = sample
-    return c
+def workload_config(cfg, T):
+    """The `config` object of the cfg2 line; both arms print the same one."""
+    return {"workload": f"{cfg.name}: Top-2 MoE layer, d_model {cfg.d_model}, "
+                        f"{cfg.num_experts} experts, d_ff {cfg.dim_ff}, {cfg.samples} packed "
+                        f"samples U{{16..256}}",
+            "tokens": T, "d_model": cfg.d_model, "experts": cfg.num_experts, "d_ff": cfg.dim_ff,
+            "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
+            "l2": "flushed (256 MiB write) before every timed step",
+            "per_gpu": "one replica"}
 
 
 # ---------------------------------------------------------------------------
@@ -412,14 +432,19 @@ def run_ours(args, world, rank, local):
 
     if rank != 0:
         return
-    cpu = None
+    cpu = cpu1 = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_moe(cfg, args.cpu_seconds)
+        # Configuration 1, the reference's CPU expert loop at its own shape
+        # (T 4096, d_model 128, 8 experts, d_ff 512): the named CPU baseline.
+        cpu1 = cpu_baseline_moe(synth.CFG1, min(args.cpu_seconds, 5.0), sample_tokens=None)
     line = {
         "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(cfg, T),
+        "timing": "value: device time per step (CUDA events), host enqueue hidden behind a "
+                  "device-side wait before each step; e2e: host copies and enqueue included",
         "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": x_h.numel() * x_h.element_size(),
                 "d2h_bytes_per_step": out_h.numel() * out_h.element_size()},
@@ -434,6 +459,7 @@ def run_ours(args, world, rank, local):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
+        "cpu_baseline_cfg1": cpu1,
     }
     print(json.dumps(line), flush=True)
 
@@ -606,41 +632,7 @@ def run_ep(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
-def cfg4_batch(seed: int = 0, samples: int = CFG4_SAMPLES):
-    """Configuration 4: 2048 packed sequences with lengths U{16..256}; every
-    token carries the 28 configuration-3 bags."""
-    from cti_b200 import synth
-
-    lens = synth.packed_lengths(samples, 16, 256, seed)
-    uo = torch.zeros(samples + 1, dtype=torch.int64)
-    uo[1:] = torch.cumsum(torch.from_numpy(lens.astype(np.int64)), 0)
-    T = int(uo[-1])
-    bb = synth.bag_batch(batch=T, seed=seed)
-    return bb, uo, T
-
-
 E2E_CHUNKS = 8  # sequence groups of the cfg4 host pipeline
-
-
-def init_cfg4_model(model, seed: int = 0):
-    """Random init of the configuration: weights and embedding rows
-    ~N(0, 0.02), biases 0, LayerNorms (1, 0); every router bias gets the
-    configuration-2 Zipf(1.2) profile."""
-    from cti_b200 import synth
-
-    g = torch.Generator().manual_seed(seed + 11)
-    with torch.no_grad():
-        for name, p in model.named_parameters():
-            if "rep_encoder.emb" in name:
-                continue
-            if "norm" in name:
-                p.fill_(1.0 if name.endswith("weight") else 0.0)
-            elif p.dim() > 1:
-                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
-            else:
-                p.zero_()
-        for i, m in enumerate(model.seq_encoder.moe):
-            m.gate.w_g.bias.copy_(synth.zipf_router_bias(m.num_experts, 1.2, seed + i))
 
 
 def run_e2e(args, world, rank, local):
@@ -652,9 +644,9 @@ def run_e2e(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    bb, uo, T = cfg4_batch(seed=rank)
-    model = build_ctr_model(bb.vocab.tolist(), attention=args.attention)
-    init_cfg4_model(model)
+    bb, uo, T = synth.cfg4_batch(seed=rank)
+    model = build_ctr_model(bb.vocab.tolist())
+    synth.init_ctr_model(model)
     model.to(dev)
     model.rep_encoder.emb.weight = torch.nn.Parameter(
         synth.embedding_table(bb.total_rows, 64, seed=rank, device=dev), requires_grad=False)
@@ -757,11 +749,12 @@ def run_e2e(args, world, rank, local):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"cfg4: CTR model forward, {CFG4_SAMPLES} packed sequences "
+        "config": {"workload": f"cfg4: CTR model forward, {synth.CFG4_SAMPLES} packed sequences "
                                f"U{{16..256}} ({T} tokens), 28 bags per token, RepEncoder "
                                "LN(1792)+Linear(1792->256), 8 x (varlen causal attention 8x32 + "
                                "Top-2 MoE 16 experts d_ff 1024), MLP head 256->128->1",
-                   "tokens": T, "ids": N, "layers": 8, "attention": enc.attention,
+                   "tokens": T, "ids": N, "layers": 8,
+                   "attention": "cti_varlen_attention (this library)",
                    "l2": "flushed (256 MiB write) before every timed step",
                    "per_gpu": "one replica"},
         "e2e": {"value": e2e_ms, "unit": "ms/batch", "h2d_bytes_per_step": h2d,
@@ -820,7 +813,7 @@ def cpu_baseline_e2e(model, bb, uo, seconds: float, sample_seqs: int = 2):
     per_call = el / n
     return {"value": per_call * (T / t_s) * 1e3, "unit": "ms/batch",
             "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{sample_seqs} of {CFG4_SAMPLES} sequences ({t_s} of {T} tokens), "
+            "sample": f"{sample_seqs} of {synth.CFG4_SAMPLES} sequences ({t_s} of {T} tokens), "
                       f"{n} calls ({el:.1f} s), scaled to the batch by tokens; fp32, "
                       "oracle/e2e_ref.py (baseline/infer.py:244-439)"}
 
@@ -957,9 +950,6 @@ def main():
                          "cfg5: expert-parallel MoE layer (strong scaling over N)")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="cfg5 expert placement over the ranks")
-    ap.add_argument("--attention", default="cti", choices=["cti", "varlen", "padded"],
-                    help="cfg4 attention: this library's kernel, PyTorch varlen flash "
-                         "attention, or SDPA on padded sequences")
     ap.add_argument("--ep-extra-slots", type=int, default=-1,
                     help="cfg5 replica slots per rank beyond E/N (-1: 0 up to 2 ranks, "
                          "max(2, E/N/2) above)")

@@ -14,7 +14,9 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
 
 // Workspace carve-up of cti_moe_layer_forward; the same function sizes it
-// (base == nullptr) and places the buffers.
+// (base == nullptr) and places the buffers.  The [2T, F] hidden activation
+// is reserved only for shapes the fused expert FFN does not take (its
+// hidden tile stays on chip).
 struct LayerWorkspace {
   int32_t* idx2;
   float* gate2;
@@ -24,8 +26,9 @@ struct LayerWorkspace {
   int32_t* perm_inv;
   int32_t* sorted_token;
   void* xperm;
-  void* hidden;
+  void* hidden;  // nullptr when the fused FFN runs
   void* y;
+  bool fused;
   size_t bytes;
 
   LayerWorkspace(void* base, int64_t T, int D, int E, int F) {
@@ -45,7 +48,8 @@ struct LayerWorkspace {
     perm_inv = static_cast<int32_t*>(take(sizeof(int32_t) * R));
     sorted_token = static_cast<int32_t*>(take(sizeof(int32_t) * R));
     xperm = take((size_t)2 * R * D);
-    hidden = take((size_t)2 * R * F);
+    fused = cti_moe_expert_ffn_fused_supported(D, F, E, R) != 0;
+    hidden = fused ? nullptr : take((size_t)2 * R * F);
     y = take((size_t)2 * R * D);
     bytes = off;
   }
@@ -128,7 +132,7 @@ extern "C" int cti_moe_layer_forward(const void* x_bf16, const float* wg, const 
   // faster than the fused kernel's in-kernel row gather,
   // cti_moe_expert_ffn_fused_gather, which would skip the copy); shapes the
   // fused kernel does not take run two grouped GEMMs.
-  const bool fused = cti_moe_expert_ffn_fused_supported(D, F, E, R) != 0;
+  const bool fused = ws.fused;
   int rc = cti_moe_router(x_bf16, wg, bg, T, D, E, renorm, ws.idx2, ws.gate2, ws.rank, ws.hist,
                           status, stream);
   if (rc) return rc;

@@ -157,11 +157,13 @@ __global__ void __launch_bounds__(256) dispatch_scatter_kernel(
           raise_status(status, CTI_ERR_BOUNDS, (int32_t)t);
         } else {
           p = make_int2((int)p0, (int)p1);
-          reinterpret_cast<int2*>(perm_inv)[t] = p;
           sorted_token[p0] = (int32_t)t;
           sorted_token[p1] = (int32_t)t;
         }
       }
+      // A token that failed a check gets (-1, -1): the combine then skips
+      // it instead of reading whatever an earlier call left in perm_inv.
+      reinterpret_cast<int2*>(perm_inv)[t] = p;
     }
     pos_s[threadIdx.x] = p;
   }

@@ -11,7 +11,8 @@
 //
 // One warp per row; lane l holds the 8-column vectors l, l+32, ... of the
 // row, so every load and store is a coalesced 16-byte access.  cols must be
-// a multiple of 256 (8 columns x 32 lanes), at most 2048.  HBM-bound:
+// a multiple of 8, at most 2048; when it is not a multiple of 256 the lanes
+// past the row's last vector sit out of the last step.  HBM-bound:
 // 2 (or 3, 4) x rows x cols x 2 bytes per launch.
 #include "common.cuh"
 
@@ -40,26 +41,31 @@ CTI_DEVICE float warp_sum(float v) {
   return v;
 }
 
-template <int VPL>  // 16-byte vectors per lane = cols / 256
+template <int VPL>  // 16-byte vectors per lane = ceil(cols / 256)
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     add_layernorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
                          const __nv_bfloat16* __restrict__ gamma,
-                         const __nv_bfloat16* __restrict__ beta, int64_t rows, float eps,
-                         __nv_bfloat16* __restrict__ sum_out, __nv_bfloat16* __restrict__ out) {
-  constexpr int C = VPL * 256;
+                         const __nv_bfloat16* __restrict__ beta, int64_t rows, int cols,
+                         float eps, __nv_bfloat16* __restrict__ sum_out,
+                         __nv_bfloat16* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + row * C);
-  const uint4* rr = r ? reinterpret_cast<const uint4*>(r + row * C) : nullptr;
+  const int nvec = cols >> 3;  // 16-byte vectors in the row
+  // Vector j*32 + lane of the row exists for every j < VPL-1; for the last
+  // step only where it is below nvec.
+  auto live = [&](int j) { return j < VPL - 1 || j * 32 + lane < nvec; };
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * cols);
+  const uint4* rr = r ? reinterpret_cast<const uint4*>(r + row * cols) : nullptr;
   float v[VPL][8];
   uint4 raw[VPL];
 #pragma unroll
-  for (int j = 0; j < VPL; ++j) raw[j] = __ldg(xr + j * 32 + lane);
+  for (int j = 0; j < VPL; ++j) raw[j] = live(j) ? __ldg(xr + j * 32 + lane) : make_uint4(0, 0, 0, 0);
   if (rr) {
     uint4 rv[VPL];
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) rv[j] = __ldg(rr + j * 32 + lane);
+    for (int j = 0; j < VPL; ++j)
+      rv[j] = live(j) ? __ldg(rr + j * 32 + lane) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       float a[8], b[8];
@@ -70,33 +76,38 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
       raw[j] = pack8(a);  // the bf16 sum is what the statistics see
     }
     if (sum_out) {
-      uint4* so = reinterpret_cast<uint4*>(sum_out + row * C);
+      uint4* so = reinterpret_cast<uint4*>(sum_out + row * cols);
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) so[j * 32 + lane] = raw[j];
+      for (int j = 0; j < VPL; ++j)
+        if (live(j)) so[j * 32 + lane] = raw[j];
     }
   }
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
-    unpack8(raw[j], v[j]);
+    unpack8(raw[j], v[j]);  // zero for vectors past the row
 #pragma unroll
     for (int i = 0; i < 8; ++i) s += v[j][i];
   }
-  const float mean = warp_sum(s) * (1.0f / C);
+  const float inv_c = 1.0f / (float)cols;
+  const float mean = warp_sum(s) * inv_c;
   float q = 0.f;
 #pragma unroll
-  for (int j = 0; j < VPL; ++j)
+  for (int j = 0; j < VPL; ++j) {
+    if (!live(j)) continue;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float d = v[j][i] - mean;
       q = fmaf(d, d, q);
     }
-  const float rstd = rsqrtf(warp_sum(q) * (1.0f / C) + eps);
+  }
+  const float rstd = rsqrtf(warp_sum(q) * inv_c + eps);
   const uint4* g4 = reinterpret_cast<const uint4*>(gamma);
   const uint4* b4 = reinterpret_cast<const uint4*>(beta);
-  uint4* o4 = reinterpret_cast<uint4*>(out + row * C);
+  uint4* o4 = reinterpret_cast<uint4*>(out + row * cols);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
+    if (!live(j)) continue;
     float g[8], b[8], y[8];
     unpack8(__ldg(g4 + j * 32 + lane), g);
     unpack8(__ldg(b4 + j * 32 + lane), b);
@@ -108,13 +119,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 
 template <int VPL>
 int launch_ln(const void* x, const void* r, const void* gamma, const void* beta, int64_t rows,
-              float eps, void* sum_out, void* out, cudaStream_t s) {
+              int cols, float eps, void* sum_out, void* out, cudaStream_t s) {
   const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (blocks > INT32_MAX) return CTI_ERR_UNSUPPORTED;
   add_layernorm_kernel<VPL><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, s>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(r),
       static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta), rows,
-      eps, static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(out));
+      cols, eps, static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError() == cudaSuccess ? CTI_OK : CTI_ERR_CUDA;
 }
 
@@ -129,7 +140,7 @@ extern "C" int cti_add_layernorm(const void* x_bf16, const void* residual_bf16,
                                  void* stream) {
   using namespace cti;
   if (rows < 0 || cols <= 0 || !(eps >= 0.0f)) return CTI_ERR_INVALID_ARG;
-  if (cols % 256 != 0 || cols > 2048) return CTI_ERR_UNSUPPORTED;
+  if (cols % 8 != 0 || cols > 2048) return CTI_ERR_UNSUPPORTED;
   if (rows == 0) return CTI_OK;
   if (!x_bf16 || !gamma_bf16 || !beta_bf16 || !out_bf16) return CTI_ERR_INVALID_ARG;
   if (sum_bf16 && !residual_bf16) return CTI_ERR_INVALID_ARG;
@@ -137,14 +148,14 @@ extern "C" int cti_add_layernorm(const void* x_bf16, const void* residual_bf16,
   for (const void* p : ptrs)
     if (p && !aligned16(p)) return CTI_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (cols / 256) {
-    case 1: return launch_ln<1>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    case 2: return launch_ln<2>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    case 3: return launch_ln<3>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    case 4: return launch_ln<4>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    case 5: return launch_ln<5>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    case 6: return launch_ln<6>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    case 7: return launch_ln<7>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
-    default: return launch_ln<8>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, eps, sum_bf16, out_bf16, s);
+  switch ((cols + 255) / 256) {
+    case 1: return launch_ln<1>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    case 2: return launch_ln<2>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    case 3: return launch_ln<3>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    case 4: return launch_ln<4>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    case 5: return launch_ln<5>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    case 6: return launch_ln<6>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    case 7: return launch_ln<7>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
+    default: return launch_ln<8>(x_bf16, residual_bf16, gamma_bf16, beta_bf16, rows, cols, eps, sum_bf16, out_bf16, s);
   }
 }

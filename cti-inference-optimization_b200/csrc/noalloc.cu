@@ -23,9 +23,18 @@
 //     launching concurrently on one device) race on the array and produce
 //     wrong results; serialise them.
 //   * The first call on each device resolves the device address of the array
-//     (cudaGetSymbolAddress, with that device current) and caches it.  Make
-//     that first call before any stream capture on that device.
+//     (cudaGetSymbolAddress, with that device current) and caches it together
+//     with the CUDA context that was current.  A later call under a different
+//     context on that device (a host that creates its own contexts with the
+//     driver API) resolves the address again for that context.  Make the
+//     first call on each device, and under each such context, before any
+//     stream capture there.  After cudaDeviceReset the cache can only tell a
+//     new primary context from the old one if the driver gives it a new
+//     handle; call this entry point again only after a fresh first call
+//     has been made outside any capture.
 #include <mutex>
+
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 
@@ -39,20 +48,48 @@ constexpr int64_t kHistInts = ((int64_t)CTI_NOALLOC_MAX_TOKENS + CTI_ROUTER_BLOC
 static __device__ __align__(256) int32_t g_route_scratch[kRankInts + kHistInts];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_mutex;
-int32_t* g_scratch_addr[kMaxDevices] = {nullptr};
 
-// Device address of g_route_scratch on the current device, resolved once.
+struct Resolved {
+  CUcontext ctx;  // the context that was current when addr was resolved
+  int32_t* addr;  // device address of g_route_scratch in that context
+};
+std::mutex g_mutex;
+Resolved g_resolved[kMaxDevices] = {};
+
+// cuCtxGetCurrent, fetched through the runtime's driver entry-point query
+// (the library has no link-time dependency on libcuda).
+PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  }
+  return fn;
+}
+
+// Device address of g_route_scratch on the current device under the current
+// context: resolved on the first call there and cached per device with the
+// context it belongs to.
 int32_t* scratch_on_current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  auto get_ctx = ctx_get_current();
+  if (get_ctx == nullptr) return nullptr;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_route_scratch) != cudaSuccess || p == nullptr) return nullptr;
-    g_scratch_addr[dev] = static_cast<int32_t*>(p);
-  }
-  return g_scratch_addr[dev];
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return nullptr;
+  Resolved& r = g_resolved[dev];
+  if (ctx != nullptr && r.addr != nullptr && r.ctx == ctx) return r.addr;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_route_scratch) != cudaSuccess || p == nullptr) return nullptr;
+  // The runtime makes the device's primary context current if none was.
+  if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return nullptr;
+  r.ctx = ctx;
+  r.addr = static_cast<int32_t*>(p);
+  return r.addr;
 }
 
 }  // namespace

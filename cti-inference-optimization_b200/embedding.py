@@ -77,10 +77,10 @@ class RepEncoder(nn.Module):
                                      self.slot_num, out_dtype=out_dtype)
 
     def forward(self, batch: dict) -> torch.Tensor:
+        """linear(input_norm(pooled)) in bf16 (the model after
+        prepare_for_inference); the LayerNorm runs on the sm_100a kernel,
+        which raises for other dtypes."""
         pooled = self.pool(batch, out_dtype=self.input_norm.weight.dtype)
-        if pooled.dtype == torch.bfloat16 and pooled.shape[1] % 256 == 0:
-            _, normed = ops.add_layernorm(pooled, None, self.input_norm.weight,
-                                          self.input_norm.bias, self.input_norm.eps)
-        else:
-            normed = self.input_norm(pooled)
+        _, normed = ops.add_layernorm(pooled, None, self.input_norm.weight,
+                                      self.input_norm.bias, self.input_norm.eps)
         return self.linear(normed)

@@ -22,11 +22,10 @@ the reference's parameter names, so a reference state dict loads as is:
     (``baseline/infer.py:686``).
 
 Attention over the packed sequences runs on this library's varlen causal
-attention kernel (``cti_varlen_attention``, head_dim 32) by default, with
-PyTorch's variable-length flash attention (``varlen``) and SDPA over padded
-sequences (``padded``) as the alternatives the tests compare it with; the
-reference builds a dense [T, T] mask instead (``get_sequence_causal_mask``,
-``baseline/infer.py:420-427``), which does not fit at T = 278k.  This module
+attention kernel (``cti_varlen_attention``, head_dim 32); the reference
+builds a dense [T, T] mask instead (``get_sequence_causal_mask``,
+``baseline/infer.py:420-427``), which does not fit at T = 278k.  There is
+no other backend: shapes the kernels do not cover raise.  This module
 is the model around the hot path; the hot path itself is the MoE layer and
 the pooling.
 """
@@ -43,45 +42,12 @@ from .embedding import RepEncoder
 from .moe import SMoE
 
 
-def varlen_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                            cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
-    """Causal attention inside each packed sequence.  q, k, v [T, H, hd]
-    (bf16, CUDA); cu_seqlens int32 [N+1]."""
-    from torch.nn.attention.varlen import varlen_attn
-
-    return varlen_attn(q, k, v, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen,
-                       window_size=(-1, 0))
-
-
-def padded_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                            cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
-    """The same through scaled_dot_product_attention on sequences padded to
-    max_seqlen.  Padding sits after each sequence's last token, so the
-    causal mask alone keeps it out of every real query."""
-    T, H, hd = q.shape
-    N = cu_seqlens.numel() - 1
-    starts = cu_seqlens[:-1].long()
-    lens = (cu_seqlens[1:] - cu_seqlens[:-1]).long()
-    seq = torch.repeat_interleave(torch.arange(N, device=q.device), lens)
-    pos = torch.arange(T, device=q.device) - starts[seq]
-
-    def pad(t):
-        out = t.new_zeros(N, max_seqlen, H, hd)
-        out[seq, pos] = t
-        return out.transpose(1, 2)
-
-    o = torch.nn.functional.scaled_dot_product_attention(pad(q), pad(k), pad(v), is_causal=True)
-    return o.transpose(1, 2)[seq, pos]
-
-
-def cti_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                         cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
-    """The same on this library's kernel (cti_varlen_attention, head_dim 32)."""
+def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
+    """Causal attention inside each packed sequence on this library's kernel
+    (cti_varlen_attention, head_dim 32).  q, k, v [T, H, hd] bf16 CUDA
+    views; cu_seqlens int32 [N+1]."""
     return ops.varlen_attention(q, k, v, cu_seqlens, max_seqlen)
-
-
-ATTENTION = {"cti": cti_causal_attention, "varlen": varlen_causal_attention,
-             "padded": padded_causal_attention}
 
 
 class SequenceGroups(NamedTuple):
@@ -138,8 +104,7 @@ class TransformerEncoder(nn.Module):
     CUDA events there)."""
 
     def __init__(self, d_model: int, n_heads: int, num_layers: int, dim_ff: int,
-                 num_experts: int = 8, activation: str = "gelu", renormalize: bool = True,
-                 attention: str = "cti"):
+                 num_experts: int = 8, activation: str = "gelu", renormalize: bool = True):
         super().__init__()
         if d_model % n_heads:
             raise ValueError("d_model must be a multiple of n_heads")
@@ -158,7 +123,6 @@ class TransformerEncoder(nn.Module):
                  renormalize=renormalize)
             for _ in range(num_layers)
         ])
-        self.attention = attention
 
     @torch.no_grad()
     def prepare_for_inference(self) -> None:
@@ -173,12 +137,9 @@ class TransformerEncoder(nn.Module):
         self._prepared = (w0.device, w0.dtype)
 
     def _add_norm(self, x, r, norm):
-        """(x + r, norm(x + r)); the fused sm_100a kernel for bf16 rows whose
-        width is a multiple of 256, torch otherwise."""
-        if x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 256 == 0:
-            return ops.add_layernorm(x, r, norm.weight, norm.bias, norm.eps)
-        s = x if r is None else x + r
-        return s, norm(s)
+        """(x + r, norm(x + r)) on the fused sm_100a kernel (bf16 rows; the
+        kernel raises for widths it does not cover)."""
+        return ops.add_layernorm(x, r, norm.weight, norm.bias, norm.eps)
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor, extension: dict):
@@ -189,7 +150,6 @@ class TransformerEncoder(nn.Module):
             self.prepare_for_inference()
         cu = extension["cu_seqlens"]
         max_len = int(extension["max_seqlen"])
-        attn = ATTENTION[self.attention]
         T = x.shape[0]
         H, hd = self.n_heads, self.head_dim
         mark = extension.get("mark") or (lambda name: None)
@@ -197,7 +157,8 @@ class TransformerEncoder(nn.Module):
         for i in range(self.num_layers):
             x, h = self._add_norm(x, pending, self.norm1[i])
             qkv = torch.nn.functional.linear(h, *self._qkv[i]).view(T, 3, H, hd)
-            a = attn(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, max_len).reshape(T, self.d_model)
+            a = causal_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, max_len).reshape(
+                T, self.d_model)
             x, h = self._add_norm(x, self.out_proj[i](a), self.norm2[i])
             mark("attention")
             moe_out, _ = self.moe[i](h.unsqueeze(0))
@@ -359,12 +320,10 @@ class CTRModel(nn.Module):
 
 def build_ctr_model(vocab_sizes, emb_dim: int = 64, slot_num: int = 28, d_model: int = 256,
                     n_heads: int = 8, num_layers: int = 8, dim_ff: int = 1024,
-                    num_experts: int = 16, head_hidden: int = 128,
-                    attention: str = "cti") -> CTRModel:
+                    num_experts: int = 16, head_hidden: int = 128) -> CTRModel:
     """The configuration-4 model: per-slot tables, 8 layers of 8 heads x 32,
     16 experts of d_ff 1024, MLP head 256 -> 128 -> 1."""
     rep = RepEncoder(vocab_size=int(sum(vocab_sizes)), emb_dim=emb_dim, padding_idx=0,
                      slot_num=slot_num, d_model=d_model, vocab_sizes=vocab_sizes)
-    enc = TransformerEncoder(d_model, n_heads, num_layers, dim_ff, num_experts,
-                             attention=attention)
+    enc = TransformerEncoder(d_model, n_heads, num_layers, dim_ff, num_experts)
     return CTRModel(rep, enc, d_model, head_hidden)

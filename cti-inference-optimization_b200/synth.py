@@ -151,7 +151,11 @@ def zipf_ids(n: int, vocab: int, s: float, rng) -> np.ndarray:
     w = np.arange(1, vocab + 1, dtype=np.float64) ** (-s)
     cdf = np.cumsum(w)
     cdf /= cdf[-1]
-    ranks = np.searchsorted(cdf, rng.random(n), side="right")
+    # torch's searchsorted runs on all host threads and returns exactly what
+    # np.searchsorted(side="right") does (the configuration-4 batch draws
+    # about 200 M ids).
+    ranks = torch.searchsorted(torch.from_numpy(cdf), torch.from_numpy(rng.random(n)),
+                               right=True).numpy()
     ranks = np.minimum(ranks, vocab - 1)
     perm = rng.permutation(vocab)
     return perm[ranks]
@@ -197,3 +201,72 @@ def embedding_table(total_rows: int, dim: int = 64, seed: int = 0, device="cpu")
         e = min(total_rows, s + step)
         out[s:e] = (torch.randn(e - s, dim, generator=g, device=device) * 0.02).half()
     return out
+
+
+# ---------------------------------------------------------------------------
+# The configuration-4 CTR model: batch and random init.
+# ---------------------------------------------------------------------------
+CFG4_SAMPLES = 2048
+
+
+def cfg4_batch(seed: int = 0, samples: int = CFG4_SAMPLES):
+    """Configuration 4: `samples` packed sequences with lengths U{16..256};
+    every token carries the 28 configuration-3 bags.  Returns (BagBatch over
+    the T tokens, int64 user_offsets [samples + 1], T)."""
+    lens = packed_lengths(samples, 16, 256, seed)
+    uo = torch.zeros(samples + 1, dtype=torch.int64)
+    uo[1:] = torch.cumsum(torch.from_numpy(lens.astype(np.int64)), 0)
+    T = int(uo[-1])
+    return bag_batch(batch=T, seed=seed), uo, T
+
+
+def init_ctr_model(model, seed: int = 0) -> None:
+    """The configuration's random init of a CTR model (reference parameter
+    names): weights ~N(0, 0.02), biases 0, LayerNorms (1, 0), and every
+    router bias the Zipf(1.2) profile.  The embedding table is left alone
+    (embedding_table() draws it)."""
+    g = torch.Generator().manual_seed(seed + 11)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "rep_encoder.emb" in name:
+                continue
+            if "norm" in name:
+                p.fill_(1.0 if name.endswith("weight") else 0.0)
+            elif p.dim() > 1:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+            else:
+                p.zero_()
+        for i, m in enumerate(model.seq_encoder.moe):
+            m.gate.w_g.bias.copy_(zipf_router_bias(m.num_experts, 1.2, seed + i))
+
+
+def sequence_subbatch(bb: BagBatch, user_offsets: torch.Tensor, seqs) -> dict:
+    """The flat-layout batch of the sequences `seqs` (ascending indices into
+    user_offsets) alone: their tokens in order, each feature's bags and ids
+    copied out.  Sequences are independent in the CTR model, so the model's
+    output on this batch equals its output on those sequences' tokens in the
+    whole batch."""
+    uo = user_offsets.long()
+    F_ = bb.features
+    T = int(uo[-1])
+    offs = bb.row_offsets.view(F_, T + 1)
+    ranges = [(int(uo[s]), int(uo[s + 1])) for s in seqs]
+    lens = [b - a for a, b in ranges]
+    new_uo = torch.zeros(len(seqs) + 1, dtype=torch.int64)
+    new_uo[1:] = torch.cumsum(torch.tensor(lens, dtype=torch.int64), 0)
+    vals, row_offs, voff = [], [], []
+    start = 0
+    for f in range(F_):
+        v0 = int(bb.val_offsets[f])
+        parts, counts = [], [torch.zeros(1, dtype=torch.int64)]
+        for a, b in ranges:
+            o = offs[f, a:b + 1]
+            parts.append(bb.values[v0 + int(o[0]):v0 + int(o[-1])])
+            counts.append(o[1:] - o[:-1])
+        fv = torch.cat(parts)
+        vals.append(fv)
+        row_offs.append(torch.cumsum(torch.cat(counts), 0))
+        voff.append(start)
+        start += fv.numel()
+    return {"_flat_values": torch.cat(vals), "_flat_row_offsets": torch.cat(row_offs),
+            "_val_offsets": torch.tensor(voff, dtype=torch.int64), "user_offsets": new_uo}

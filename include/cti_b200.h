@@ -126,7 +126,10 @@ int cti_moe_dispatch(const void* x_bf16, const int32_t* idx2, const int32_t* rou
  * CTI_ERR_UNSUPPORTED).  All calls on a device share the array, so calls
  * that overlap on the GPU race; serialise them.  The first call on each
  * device resolves the array's address and should come before any stream
- * capture.
+ * capture.  The address is cached per device together with the CUDA
+ * context that was current; a call under another context (one the host
+ * made with the driver API) resolves it again, so make the first call
+ * under each such context outside any capture as well.
  * ---------------------------------------------------------------------- */
 #define CTI_NOALLOC_MAX_TOKENS 131072
 #define CTI_NOALLOC_MAX_EXPERTS 128
@@ -282,7 +285,8 @@ int cti_varlen_attention(const void* q_bf16, const void* k_bf16, const void* v_b
  *   out = bf16((s - mean) * rsqrt(var + eps) * gamma + beta), fp32 mean and
  *         biased variance of the bf16 row s
  * bf16 [rows, cols] row-major, gamma / beta bf16 [cols]; cols a multiple of
- * 256, at most 2048; every pointer 16-byte aligned.
+ * 8, at most 2048 (CTI_ERR_UNSUPPORTED otherwise); every pointer 16-byte
+ * aligned.
  * ---------------------------------------------------------------------- */
 int cti_add_layernorm(const void* x_bf16, const void* residual_bf16, const void* gamma_bf16,
                       const void* beta_bf16, int64_t rows, int cols, float eps, void* sum_bf16,

@@ -15,8 +15,8 @@ Contents:
   router_order.c     the router restated in C with the kernel's fixed
                      reduction order (one fmaf chain per logit), for a
                      strict bit-exact check of expert indices.
-  model_ref.py       the reference model skeleton (baseline/infer.py:
-                     244-439) at the end-to-end configuration.
+  e2e_ref.py         the reference CTR model graph (baseline/infer.py:
+                     244-439) in fp32 at the end-to-end configuration.
   build.py           compiles router_order.c into _build/liborder.so.
 
 Pinning: tests/golden/ holds fixtures produced by running the reference's

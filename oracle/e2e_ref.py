@@ -49,7 +49,9 @@ def ctr_forward_ref(sd: dict, batch: dict, *, slot_num: int, n_heads: int, num_l
                     num_experts: int, table_row_base=None, vocab=None):
     """Returns (encoder output [T, D], clamped logits [T], probabilities [T]),
     all fp32.  ``sd`` maps reference parameter names to tensors."""
-    g = {k: v.float() for k, v in sd.items()}
+    # The embedding table stays in its own dtype: the pooling upcasts only
+    # the rows it gathers.
+    g = {k: v.float() for k, v in sd.items() if k != "rep_encoder.emb.weight"}
     table = sd["rep_encoder.emb.weight"]
     if table_row_base is None:  # one shared table, as in the reference
         table_row_base = torch.zeros(slot_num, dtype=torch.int64)

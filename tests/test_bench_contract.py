@@ -15,11 +15,23 @@ REQUIRED = {
 }
 
 
+# Runs the reference arm in-process, then reports whether this repository's
+# library or package was ever loaded into that process.
+_RUN_REFERENCE_ARM = """
+import runpy, sys
+sys.argv = ["bench.py", "--impl", "reference", "--steps", "3", "--warmup", "3"]
+runpy.run_path("bench.py", run_name="__main__")
+maps = open("/proc/self/maps").read()
+print("LOADED_LIB", "libcti_b200" in maps, "PACKAGE", "cti_b200" in sys.modules)
+"""
+
+
 def test_reference_arm_prints_one_contract_line():
-    proc = subprocess.run(
-        [sys.executable, "bench.py", "--impl", "reference", "--steps", "3", "--warmup", "3"],
-        cwd=ROOT, capture_output=True, text=True, timeout=600)
+    proc = subprocess.run([sys.executable, "-c", _RUN_REFERENCE_ARM], cwd=ROOT,
+                          capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stderr[-2000:]
+    # The reference arm runs only the reference's CPU code path.
+    assert "LOADED_LIB False PACKAGE False" in proc.stdout, proc.stdout
     lines = [l for l in proc.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1, proc.stdout
     d = json.loads(lines[0])
@@ -32,6 +44,12 @@ def test_reference_arm_prints_one_contract_line():
     assert d["n_gpus"] == 1 and d["steps"] == 3 and d["warmup"] == 3
     assert d["higher_is_better"] is True and d["value"] > 0
     assert d["config"]["tokens"] == 72214 and "workload" in d["config"]
+    # The same config object as our arm's line: the whole batch, no sample.
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    synth = bench.load_synth()
+    assert d["config"] == bench.workload_config(synth.CFG2, 72214)
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert "sample" in cb

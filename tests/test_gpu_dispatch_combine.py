@@ -78,3 +78,22 @@ def test_combine_rejects_out_of_range_positions(cuda_device):
     ops.combine(y, perm_inv, gate2)
     code, detail = _lib.read_status(cuda_device)
     assert code == _lib.CTI_ERR_BOUNDS and detail == 7
+
+
+def test_dispatch_marks_rejected_tokens_in_perm_inv(cuda_device):
+    """A route whose expert id is out of range (planted on the host after
+    routing) is reported as CTI_ERR_BOUNDS with its token, and that token's
+    perm_inv entry is (-1, -1), so the combine skips it deterministically
+    instead of reading stale positions."""
+    from cti_b200 import _lib, ops
+
+    T, D, E = 500, 128, 8
+    x, xd, r = _route(T, D, E, cuda_device, seed=4)
+    r.idx2[123, 1] = E  # one past the last expert
+    d = ops.dispatch(xd, r, E)
+    code, detail = _lib.read_status(cuda_device)
+    assert code == _lib.CTI_ERR_BOUNDS and detail == 123
+    assert d.perm_inv[123].tolist() == [-1, -1]
+    ok = torch.ones(T, dtype=torch.bool)
+    ok[123] = False
+    assert (d.perm_inv.cpu()[ok] >= 0).all()

@@ -14,14 +14,14 @@ pytestmark = pytest.mark.gpu
 STRESS_MAX_REL_ERR = 5e-2
 
 
-def _build(name, dev, attention):
+def _build(name, dev):
     import cti_b200
     from cti_b200.model import CTRModel, TransformerEncoder
 
     N, Lmax, D, H, L, Fd, E, V, _ = gi.E2E_CASES[name]
     rep = cti_b200.RepEncoder(vocab_size=V, emb_dim=gi.E2E_EMB, padding_idx=0,
                               slot_num=gi.E2E_SLOTS, d_model=D)
-    enc = TransformerEncoder(D, H, L, Fd, num_experts=E, attention=attention)
+    enc = TransformerEncoder(D, H, L, Fd, num_experts=E)
     model = CTRModel(rep, enc, D, head_hidden=gi.E2E_HEAD)
     batch, sd = gi.e2e_inputs(name)
     model.load_state_dict(sd, strict=True)
@@ -29,9 +29,8 @@ def _build(name, dev, attention):
     return model, batch, sd
 
 
-@pytest.mark.parametrize("attention", ["cti", "varlen", "padded"])
 @pytest.mark.parametrize("name", list(gi.E2E_CASES))
-def test_ctr_model_matches_reference_fixture(cuda_device, attention, name):
+def test_ctr_model_matches_reference_fixture(cuda_device, name):
     """Configuration init (weight std 0.02): encoder output within max rel
     err 2e-2 and probabilities within 1e-3 absolute.
     Large-weight stress case (weights 2.5-5x the configuration's, logits of
@@ -40,7 +39,7 @@ def test_ctr_model_matches_reference_fixture(cuda_device, attention, name):
     not 1e-3 in probability."""
     from cti_b200 import _lib
 
-    model, batch, sd = _build(name, cuda_device, attention)
+    model, batch, sd = _build(name, cuda_device)
     gold = load_golden(name)
     assert str(gold["input_sha256"]) == gi.e2e_digest(batch, sd)
     hidden = {}
@@ -61,11 +60,12 @@ def test_ctr_model_matches_reference_fixture(cuda_device, attention, name):
         assert max_rel_err(logits.float().reshape(-1).cpu(), torch.from_numpy(gold["logits"])) < tol
 
 
-def test_ctr_model_attention_backends_agree(cuda_device):
-    """This library's kernel, varlen flash attention and padded SDPA on a
-    larger packed batch."""
-    from cti_b200.model import (cti_causal_attention, padded_causal_attention,
-                                varlen_causal_attention)
+def test_attention_kernel_agrees_with_torch_formulations(cuda_device):
+    """The model's attention (this library's kernel) against PyTorch's
+    varlen flash attention and padded SDPA (tests/attention_ref.py) on a
+    larger packed batch, and one sequence against a plain fp32 softmax."""
+    from attention_ref import padded_causal_attention, varlen_causal_attention
+    from cti_b200.model import causal_attention
 
     g = torch.Generator().manual_seed(3)
     lens = torch.randint(1, 257, (64,), generator=g)
@@ -76,7 +76,7 @@ def test_ctr_model_attention_backends_agree(cuda_device):
     cu = cu.to(cuda_device)
     a = varlen_causal_attention(q, k, v, cu, 256).float()
     b = padded_causal_attention(q, k, v, cu, 256).float()
-    c = cti_causal_attention(q, k, v, cu, 256).float()
+    c = causal_attention(q, k, v, cu, 256).float()
     assert max_rel_err(a, b) < 1e-2
     assert max_rel_err(c, b) < 1e-2
     # one sequence against a plain fp32 softmax
@@ -87,6 +87,7 @@ def test_ctr_model_attention_backends_agree(cuda_device):
                         float("-inf"))
     ref = (torch.softmax(sc, -1) @ vs).transpose(0, 1)
     assert max_rel_err(a[s0:s1], ref) < 1e-2
+    assert max_rel_err(c[s0:s1], ref) < 1e-2
 
 
 def test_cfg4_shaped_model_matches_oracle(cuda_device):
@@ -94,14 +95,8 @@ def test_cfg4_shaped_model_matches_oracle(cuda_device):
     experts of d_ff 1024 with the Zipf router bias, per-slot tables, weights
     ~N(0, 0.02)) at 2 layers and 24 sequences, against the oracle:
     probabilities within 1e-3 absolute."""
-    import sys
-    from pathlib import Path
-
     from cti_b200 import _lib, synth
     from cti_b200.model import build_ctr_model
-
-    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
-    import bench
 
     nseq = 24
     lens = torch.randint(16, 257, (nseq,), generator=torch.Generator().manual_seed(1))
@@ -110,7 +105,7 @@ def test_cfg4_shaped_model_matches_oracle(cuda_device):
     T = int(uo[-1])
     bb = synth.bag_batch(batch=T, seed=2, vocab_lo=1e3, vocab_hi=2e4)
     model = build_ctr_model(bb.vocab.tolist(), num_layers=2)
-    bench.init_cfg4_model(model)
+    synth.init_ctr_model(model)
     with torch.no_grad():
         model.rep_encoder.emb.weight.copy_(synth.embedding_table(bb.total_rows, 64, seed=2).float())
         for name, p in model.named_parameters():
@@ -136,14 +131,8 @@ def test_predict_host_chunks_match_predict(cuda_device):
     predict on the device batch and against the oracle: probabilities within
     1e-3 absolute, for 1, 3 and 7 chunks and a repeated call into the same
     output.  Zero-length bags and a 1-token sequence are included."""
-    import sys
-    from pathlib import Path
-
     from cti_b200 import _lib, synth
     from cti_b200.model import build_ctr_model
-
-    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
-    import bench
 
     g = torch.Generator().manual_seed(11)
     lens = torch.randint(16, 257, (20,), generator=g)
@@ -153,7 +142,7 @@ def test_predict_host_chunks_match_predict(cuda_device):
     T = int(uo[-1])
     bb = synth.bag_batch(batch=T, seed=5, vocab_lo=1e3, vocab_hi=2e4)
     model = build_ctr_model(bb.vocab.tolist(), num_layers=2)
-    bench.init_cfg4_model(model, seed=5)
+    synth.init_ctr_model(model, seed=5)
     with torch.no_grad():
         model.rep_encoder.emb.weight.copy_(synth.embedding_table(bb.total_rows, 64, seed=5).float())
         for name, p in model.named_parameters():
@@ -180,3 +169,45 @@ def test_predict_host_chunks_match_predict(cuda_device):
         np.testing.assert_allclose(probs.numpy(), dev_probs, rtol=0, atol=1e-3)
         np.testing.assert_allclose(probs.numpy(), ref.numpy(), rtol=0, atol=1e-3)
         out = probs
+
+
+def test_full_cfg4_model_matches_oracle_on_sampled_sequences(cuda_device):
+    """The whole configuration-4 forward: 2048 packed sequences (284,237
+    tokens, 204 M ids), 8 layers, per-slot fp16 tables, run on the device
+    as the benchmark runs it.  Sequences are independent, so the oracle
+    runs on 24 seeded sampled sequences alone (their flat-layout sub-batch)
+    and their probabilities must agree within 1e-3 absolute."""
+    from cti_b200 import _lib, synth
+    from cti_b200.model import build_ctr_model
+
+    bb, uo, T = synth.cfg4_batch(seed=0)
+    model = build_ctr_model(bb.vocab.tolist())
+    synth.init_ctr_model(model)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "gate" not in name and "emb" not in name:
+                p.copy_(p.bfloat16().float())
+    # Everything but the 1.4 GB table goes to the oracle in fp32.
+    sd = {k: v.clone() for k, v in model.state_dict().items() if k != "rep_encoder.emb.weight"}
+    model.rep_encoder.emb.weight = torch.nn.Parameter(torch.empty(0), requires_grad=False)
+    table = synth.embedding_table(bb.total_rows, 64, seed=0)
+    model.to(cuda_device)
+    model.rep_encoder.emb.weight = torch.nn.Parameter(table.to(cuda_device), requires_grad=False)
+    model.prepare_for_inference()
+    batch = {"_flat_values": bb.values, "_flat_row_offsets": bb.row_offsets,
+             "_val_offsets": bb.val_offsets, "user_offsets": uo}
+    probs = model.predict({k: v.to(cuda_device) for k, v in batch.items()}).cpu()
+    _lib.raise_on_status(cuda_device)
+    assert probs.shape == (T,) and torch.isfinite(probs).all()
+
+    seqs = sorted(torch.randperm(synth.CFG4_SAMPLES,
+                                 generator=torch.Generator().manual_seed(7))[:24].tolist())
+    sub = synth.sequence_subbatch(bb, uo, seqs)
+    sd["rep_encoder.emb.weight"] = table
+    torch.set_num_threads(8)
+    _, _, ref = e2e_ref.ctr_forward_ref(sd, sub, slot_num=28, n_heads=8, num_layers=8,
+                                        num_experts=16, table_row_base=bb.table_row_base,
+                                        vocab=bb.vocab)
+    mine = torch.cat([probs[int(uo[s]):int(uo[s + 1])] for s in seqs])
+    assert mine.numel() == ref.numel() == int(sub["user_offsets"][-1])
+    np.testing.assert_allclose(mine.numpy(), ref.numpy(), rtol=0, atol=1e-3)

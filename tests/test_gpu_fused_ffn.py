@@ -1,5 +1,5 @@
 """Stage 3 fused expert FFN (fc1 -> GELU -> fc2 with the hidden tile kept in
-shared memory) on the B200 vs a torch fp32 reference of the same op.
+tensor memory) on the B200 vs a torch fp32 reference of the same op.
 Tolerance: max rel err 1e-2 (bf16 hidden activations and bf16 output vs
 fp32 throughout)."""
 import pytest

@@ -43,7 +43,28 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("rows,K,N,sizes,Gw,act", CASES)
+def zipf_sizes(total, groups, s=1.2, seed=0):
+    """Group sizes with a Zipf(s) profile over a seeded order, summing to
+    `total` (some groups may get 0 rows)."""
+    g = torch.Generator().manual_seed(seed)
+    p = (torch.randperm(groups, generator=g).double() + 1.0) ** (-s)
+    sizes = torch.floor(p / p.sum() * total).long()
+    sizes[0] += total - int(sizes.sum())
+    return sizes.tolist()
+
+
+# The two expert GEMMs of configuration 5 (d_model 1024, d_ff 4096, 64
+# experts): fc1 K 1024 -> N 4096 with GELU, fc2 K 4096 -> N 1024, ragged
+# Zipf-sized groups over all 64 experts (weights of 16 distinct experts,
+# group g uses g % 16).
+CFG5_CASES = [
+    (6000, 1024, 4096, zipf_sizes(6000, 64, seed=1), 16, "gelu"),
+    (6000, 4096, 1024, zipf_sizes(6000, 64, seed=2), 16, "none"),
+    (2311, 1024, 4096, zipf_sizes(2311, 64, seed=3), 16, "relu"),
+]
+
+
+@pytest.mark.parametrize("rows,K,N,sizes,Gw,act", CASES + CFG5_CASES)
 def test_grouped_gemm_matches_fp32(cuda_device, rows, K, N, sizes, Gw, act):
     from cti_b200 import _lib, ops
 

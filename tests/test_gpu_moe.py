@@ -80,6 +80,32 @@ def test_smoe_matches_oracle_at_benchmark_shape(cuda_device, cfg_name, fused):
     assert torch.equal(idx[0].cpu()[ok], g.idx[ok])
 
 
+def test_smoe_matches_oracle_at_cfg5_shape(cuda_device):
+    """Configuration 5's layer shape (d_model 1024, 64 experts, d_ff 4096,
+    Zipf(1.2) router bias) on one GPU over 8,192 tokens - the unfused
+    grouped-GEMM path the expert-parallel layer runs on every rank - against
+    the oracle: max rel err 2e-2, indices exact outside the near-tie band."""
+    from cti_b200 import _lib, synth
+    import cti_b200
+
+    cfg = synth.CFG5
+    T = 8192
+    w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, seed=4)
+    x = synth.moe_activations(T, cfg.d_model, seed=4)
+    m = cti_b200.SMoE(cfg.d_model, cfg.dim_ff, cfg.num_experts)
+    synth.load_moe_module(m, w)
+    m.to(cuda_device).prepare_for_inference()
+    xd = x.to(cuda_device)
+    out = m(xd.unsqueeze(0))[0][0]
+    _lib.raise_on_status(cuda_device)
+    ref, g = mr.smoe_ref(x.float(), w.wg, w.bg, w.w1.float(), w.b1, w.w2.float(), w.b2)
+    err = max_rel_err(out, ref)
+    assert err < MOE_MAX_REL_ERR, err
+    idx, _ = m.gate(xd.unsqueeze(0))
+    ok = ~mr.near_tie_mask(x.float(), w.wg, w.bg)
+    assert torch.equal(idx[0].cpu()[ok], g.idx[ok])
+
+
 def test_smoe_stages_agree_with_layer_call(cuda_device):
     from cti_b200 import _lib, synth
     import cti_b200

@@ -127,3 +127,28 @@ def test_sequence_groups_rebuild_the_batch(chunks):
         assert cu[0] == 0 and cu[-1] == n
         np.testing.assert_array_equal(cu, uo[s0:s1 + 1].numpy() - a)
     assert torch.equal(torch.cat(parts), full)
+
+
+def test_sequence_subbatch_pools_like_the_whole_batch():
+    """synth.sequence_subbatch (the oracle's sample of a configuration-4
+    batch): pooling the sub-batch gives, bit for bit, the rows of the
+    sampled sequences' tokens in the pooling of the whole batch; zero-length
+    bags and a 1-token sequence included."""
+    from cti_b200 import synth
+    from oracle.embbag_ref import embbag_ref
+
+    lens = torch.tensor([5, 1, 9, 3, 7, 2])
+    uo = torch.zeros(lens.numel() + 1, dtype=torch.int64)
+    uo[1:] = torch.cumsum(lens, 0)
+    T = int(uo[-1])
+    bb = synth.bag_batch(batch=T, seed=3, vocab_lo=50, vocab_hi=400, lam_lo=0.5, lam_hi=4)
+    table = synth.embedding_table(bb.total_rows, 8, seed=3)
+    full = embbag_ref(bb.values, bb.row_offsets, bb.val_offsets, table, bb.table_row_base,
+                      bb.vocab, bb.features)
+    seqs = [1, 2, 5]
+    sub = synth.sequence_subbatch(bb, uo, seqs)
+    assert sub["user_offsets"].tolist() == [0, 1, 10, 12]
+    pooled = embbag_ref(sub["_flat_values"], sub["_flat_row_offsets"], sub["_val_offsets"],
+                        table, bb.table_row_base, bb.vocab, bb.features)
+    rows = torch.cat([torch.arange(int(uo[s]), int(uo[s + 1])) for s in seqs])
+    assert torch.equal(pooled, full[rows])
