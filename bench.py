@@ -17,7 +17,13 @@ roofline  the dominant kernel (the expert FFN GEMM) timed alone with CUDA
        events: algorithmic FLOPs / mean launch time vs the measured bf16 peak.
 cpu_baseline  the reference's PyTorch CPU expert loop (oracle port of
        baseline/infer.py:280-358, fp32) on a bounded token sample, rank 0,
-       N=1 only.
+       N=1 only; cpu_baseline_cfg1 the same loop at configuration 1.
+ep     configuration 5 at this N (expert parallelism over the N ranks, T =
+       262,144 tokens in total, strong scaling): "even" is the
+       configuration's even sharding of the 64 experts, "replicas" (N >= 2)
+       the placement that replicates the heaviest experts.
+e2e_model  configuration 4 at N = 1: the 8-layer CTR model forward, ms per
+       batch, with inputs on the device and with the host copies.
 
 Other workloads (--config): cfg3 the 28-feature embedding-bag pooling
 (GB/s); cfg4 the whole CTR model forward (ms per batch); cfg5 the
@@ -53,6 +59,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 L2_FLUSH_BYTES = 256 << 20
 CPU_SAMPLE_TOKENS = 8192
 CALIBRATION_TOKENS = 65536
+EP_STEPS, EP_WARMUP = 10, 3      # the cfg5 and cfg4 measurements of the default line
+E2E_MODEL_STEPS = 5
 
 
 def load_peaks():
@@ -430,6 +438,31 @@ def run_ours(args, world, rank, local):
     kernel_names = {"ffn_fused": "fused_ffn_kernel", "ffn_fc1": "grouped_gemm_kernel (fc1)",
                     "ffn_fc2": "grouped_gemm_kernel (fc2)"}
 
+    # Configuration 5 at this N (expert parallelism, strong scaling): the
+    # configuration's even sharding, and from N = 2 on the placement with
+    # replicas of the heaviest experts beside it.
+    ep = None
+    if not args.no_ep:
+        ep = {"config": cfg5_config(world),
+              "even": measure_ep(args, world, rank, local, flush, "contiguous", EP_STEPS,
+                                 EP_WARMUP)}
+        if world > 1:
+            ep["replicas"] = measure_ep(args, world, rank, local, flush, "balanced", EP_STEPS,
+                                        EP_WARMUP)
+    # Configuration 4 at N = 1: the 8-layer CTR model forward, ms per batch.
+    e2e_model = None
+    if world == 1 and not args.no_e2e_model:
+        r4 = measure_e2e_model(args, world, rank, local, flush, E2E_MODEL_STEPS, EP_WARMUP)
+        e2e_model = {"metric": "e2e_forward_ms_per_batch", "unit": "ms/batch",
+                     "value": r4["ms_per_batch"], "config": cfg4_config(r4["tokens"], r4["ids"]),
+                     "with_host_copies": {"value": r4["e2e_ms_per_batch"], "unit": "ms/batch",
+                                          "h2d_bytes_per_step": r4["h2d_bytes_per_step"],
+                                          "d2h_bytes_per_step": r4["d2h_bytes_per_step"],
+                                          "chunks": r4["chunks"]},
+                     "stages_ms": r4["stages_ms"], "tokens_per_s": r4["tokens_per_s"],
+                     "expert_ffn_roofline": r4["roofline"], "pooling": r4["pooling"],
+                     "steps": E2E_MODEL_STEPS, "warmup": EP_WARMUP}
+
     if rank != 0:
         return
     cpu = cpu1 = None
@@ -460,31 +493,34 @@ def run_ours(args, world, rank, local):
         "clocks": clocks,
         "cpu_baseline": cpu,
         "cpu_baseline_cfg1": cpu1,
+        "ep": ep,
+        "e2e_model": e2e_model,
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ep(args, world, rank, local):
-    """--config cfg5: the expert-parallel layer (d_model 1024, 64 experts,
-    d_ff 4096) over T = 262,144 tokens in total, split evenly across the N
-    ranks; rank r owns experts [r*64/N, (r+1)*64/N).  Total work is fixed as
-    N grows (strong scaling); N = 1 is the single-GPU baseline (no
-    exchange)."""
-    from cti_b200 import _lib, synth
+def measure_ep(args, world, rank, local, flush, placement_kind: str, steps: int, warmup: int,
+               sampler=None) -> dict:
+    """Configuration 5 on the expert-parallel layer (d_model 1024, 64
+    experts, d_ff 4096) over T = 262,144 tokens in total, split evenly across
+    the N ranks (strong scaling).  placement_kind "contiguous": rank r owns
+    experts [r*64/N, (r+1)*64/N), the configuration's even sharding;
+    "balanced": slots placed by routing counts of a separate calibration
+    batch, with replicas of the heaviest experts from N = 4 on.  Every rank
+    calls this with the same arguments (collectives inside); the returned
+    dict is complete on rank 0."""
+    from cti_b200 import _lib, ops, synth
     from cti_b200.ep import ExpertParallelSMoE, balanced_placement
 
     dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     cfg = synth.CFG5
     T = cfg.tokens
     D, E, F = cfg.d_model, cfg.num_experts, cfg.dim_ff
     w = synth.moe_weights(D, E, F, cfg.zipf_bias, seed=0, device=dev)
     placement = None
-    if args.placement == "balanced" and world > 1:
-        # Calibrate on a separate batch (seed 1): its routing counts,
-        # summed over the ranks, give each expert's expected load.
-        from cti_b200 import ops
-
+    if placement_kind == "balanced" and world > 1:
+        # Calibrate on a separate batch (seed 1): its routing counts, summed
+        # over the ranks, give each expert's expected load.
         xc = synth.moe_activations(CALIBRATION_TOKENS, D, seed=1, device=dev)
         rc = ops.router(xc, w.wg.float().contiguous(), w.bg.float().contiguous())
         load = torch.bincount(rc.idx2.reshape(-1).long(), minlength=E).to(torch.float64)
@@ -502,27 +538,23 @@ def run_ep(args, world, rank, local):
     del w
     lo, hi = rank * T // world, (rank + 1) * T // world
     x = synth.moe_activations(T, D, seed=0, device=dev)[lo:hi].clone()
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     torch.cuda.empty_cache()
+    overlap = args.ep_exchange == "p2p"
 
-    for _ in range(args.warmup):
-        m(x)
+    for _ in range(warmup):
+        m(x, overlap=overlap)
     torch.cuda.synchronize(dev)
     _lib.raise_on_status(dev)
-
-    sampler = ClockSampler(dev) if rank == 0 else None
     barrier(world)
     torch.cuda.synchronize(dev)
     if sampler:
         sampler.start()
-    overlap = args.ep_exchange == "p2p"
-    times = time_steps(lambda: m(x, overlap=overlap), args.steps, flush, dev)
+    times = time_steps(lambda: m(x, overlap=overlap), steps, flush, dev)
     torch.cuda.synchronize(dev)
     barrier(world)
     clocks = sampler.stop() if sampler else None
     _lib.raise_on_status(dev)
     step_ms = max_over_ranks(statistics.mean(times), world, dev)
-    value = T / (step_ms / 1e3)
 
     # End to end: this rank's tokens from pinned host memory, output back.
     x_h = x.cpu().pin_memory()
@@ -534,11 +566,11 @@ def run_ep(args, world, rank, local):
         out, _ = m(x_d, overlap=overlap)
         out_h.copy_(out, non_blocking=True)
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         e2e_step()
     barrier(world)
     torch.cuda.synchronize(dev)
-    e2e_times = time_steps(e2e_step, args.steps, flush, dev, hide_host=False)
+    e2e_times = time_steps(e2e_step, steps, flush, dev, hide_host=False)
     barrier(world)
     e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
 
@@ -546,7 +578,6 @@ def run_ep(args, world, rank, local):
     # a few forwards, per rank; rows = rows this rank's experts computed.
     names = ["router", "dispatch", "exchange", "experts", "exchange_back", "combine"]
     per = {n: [] for n in names}
-    rows_local = 0
     for _ in range(5):
         flush.zero_()
         evs = [torch.cuda.Event(enable_timing=True)]
@@ -562,7 +593,6 @@ def run_ep(args, world, rank, local):
         for n, a, b in zip(names, evs[:-1], evs[1:]):
             per[n].append(a.elapsed_time(b))
     stages = {n: statistics.median(v) for n, v in per.items()}
-    from cti_b200 import ops
     r = ops.router(x, m._wg, m._bg)
     cnt = torch.bincount(r.idx2.reshape(-1).long(), minlength=E).to(torch.float64)
     if world > 1:
@@ -571,13 +601,14 @@ def run_ep(args, world, rank, local):
         dist.all_reduce(cnt)
     S = m.slots_per_rank
     nrep = torch.tensor([m.n_rep[e] for e in m.placement], dtype=torch.float64, device=dev)
-    # router outputs are dispatch positions
-    pos = torch.tensor([m.position[e] for e in m.placement], device=dev)
-    share = cnt[pos] / nrep
+    pos = torch.tensor([m.position[e] for e in m.placement], device=dev)  # router outputs
+    share = cnt[pos] / nrep                                               # are dispatch positions
     rows_per_rank = share.view(world, S).sum(dim=1).tolist()
     rows_local = rows_per_rank[rank]
     exp_ms = torch.tensor([stages["experts"]], dtype=torch.float64, device=dev)
     if world > 1:
+        import torch.distributed as dist
+
         gathered = [torch.empty_like(exp_ms) for _ in range(world)]
         dist.all_gather(gathered, exp_ms)
         experts_ms = [float(t.item()) for t in gathered]
@@ -588,45 +619,87 @@ def run_ep(args, world, rank, local):
     peaks, peak_src = load_peaks()
     peak = float(peaks["bf16_tflops"])
     total_flops = 4.0 * 2 * T * D * F
+    exchange_ms = stages["exchange"] + stages["exchange_back"]
+    del m, x, x_d
+    torch.cuda.empty_cache()
+    return {
+        "tokens_per_s": T / (step_ms / 1e3), "ms_per_step": step_ms,
+        "e2e_tokens_per_s": T / (e2e_ms / 1e3), "e2e_ms_per_step": e2e_ms,
+        "h2d_bytes_per_step": x_h.numel() * x_h.element_size() * world,
+        "d2h_bytes_per_step": out_h.numel() * out_h.element_size() * world,
+        "placement": ("contiguous (even sharding, E/N experts per rank)" if placement is None else
+                      f"balanced (LPT over the routing counts of a separate "
+                      f"{CALIBRATION_TOKENS}-token calibration batch), "
+                      f"{len(placement) // world} slots per rank, {len(placement) - E} replicas"),
+        "exchange": ("none (one rank)" if world == 1 else
+                     "counts: NCCL all_to_all_single; rows: NCCL point-to-point per peer, "
+                     "overlapped with the experts over the rows a rank routes to itself; "
+                     "results back the same way" if overlap else
+                     "NCCL all_to_all_single (counts, then rows with uneven splits; the same "
+                     "back)"),
+        "stages_ms_rank0": stages,
+        "exchange_share_rank0": exchange_ms / max(sum(stages.values()), 1e-9),
+        "rows_per_rank": rows_per_rank,
+        "experts_ms_per_rank": experts_ms,
+        "experts_roofline_rank0": {"kernel": "grouped_gemm_kernel (fc1 + fc2)",
+                                   "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                                   "frac": achieved / peak,
+                                   "peak_source": f"bf16_tflops of {peak_src}",
+                                   "flops": flops_local},
+        "layer_roofline_frac": total_flops / (step_ms / 1e3) / 1e12 / world / peak,
+        "clocks": clocks,
+    }
+
+
+def cfg5_config(world: int) -> dict:
+    from cti_b200 import synth
+
+    cfg = synth.CFG5
+    return {"workload": f"cfg5: expert-parallel Top-2 MoE layer, d_model {cfg.d_model}, "
+                        f"{cfg.num_experts} experts, d_ff {cfg.dim_ff}, {cfg.tokens} tokens in "
+                        "total split evenly over the ranks",
+            "tokens": cfg.tokens, "d_model": cfg.d_model, "experts": cfg.num_experts,
+            "d_ff": cfg.dim_ff, "parallelism": f"ep{world}", "router_bias": "zipf(1.2)",
+            "activation": "gelu", "gates": "renormalised",
+            "l2": "flushed (256 MiB write) before every timed step"}
+
+
+def run_ep(args, world, rank, local):
+    """--config cfg5: the expert-parallel layer alone (strong scaling over N;
+    N = 1 is the single-GPU baseline, no exchange)."""
+    from cti_b200 import synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    sampler = ClockSampler(dev) if rank == 0 else None
+    r = measure_ep(args, world, rank, local, flush, args.placement, args.steps, args.warmup,
+                   sampler)
     if rank != 0:
         return
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_moe(cfg, args.cpu_seconds, sample_tokens=1024)
+        cpu = cpu_baseline_moe(synth.CFG5, args.cpu_seconds, sample_tokens=1024)
+    cfg = cfg5_config(world)
+    cfg["placement"] = r["placement"]
+    cfg["exchange"] = r["exchange"]
     line = {
-        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": f"cfg5: expert-parallel Top-2 MoE layer, d_model {D}, {E} experts, "
-                               f"d_ff {F}, {T} tokens in total split evenly over the ranks",
-                   "tokens": T, "d_model": D, "experts": E, "d_ff": F,
-                   "parallelism": f"ep{world}",
-                   "placement": "contiguous" if placement is None else
-                   f"balanced (LPT over the routing counts of a separate {CALIBRATION_TOKENS}-token "
-                   f"calibration batch), {len(placement) // world} slots per rank, "
-                   f"{len(placement) - E} replicas",
-                   "exchange": ("none (one rank)" if world == 1 else
-                                "counts: NCCL all_to_all_single; rows: NCCL point-to-point per "
-                                "peer, overlapped with the experts over the rows a rank routes to "
-                                "itself; results back the same way" if overlap else
-                                "NCCL all_to_all_single (counts, then rows with uneven splits; "
-                                "the same back)"),
-                   "router_bias": "zipf(1.2)", "activation": "gelu", "gates": "renormalised",
-                   "l2": "flushed (256 MiB write) before every timed step"},
-        "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": x_h.numel() * x_h.element_size() * world,
-                "d2h_bytes_per_step": out_h.numel() * out_h.element_size() * world},
-        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel (fc1 + fc2, rank 0)",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "peak_source": f"bf16_tflops of {peak_src}",
-                     "flops_per_launch": flops_local / 2, "traffic": None},
-        "layer_roofline_frac": total_flops / (step_ms / 1e3) / 1e12 / world / peak,
-        "stages_ms_rank0": stages,
-        "rows_per_rank": rows_per_rank,
-        "experts_ms_per_rank": experts_ms,
+        "metric": "moe_layer_tokens_per_s", "value": r["tokens_per_s"], "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+        "e2e": {"value": r["e2e_tokens_per_s"], "unit": "tokens/s",
+                "ms_per_step": r["e2e_ms_per_step"],
+                "h2d_bytes_per_step": r["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": r["d2h_bytes_per_step"]},
+        "roofline": dict(r["experts_roofline_rank0"], bound="tensor", traffic=None),
+        "layer_roofline_frac": r["layer_roofline_frac"],
+        "stages_ms_rank0": r["stages_ms_rank0"],
+        "exchange_share_rank0": r["exchange_share_rank0"],
+        "rows_per_rank": r["rows_per_rank"],
+        "experts_ms_per_rank": r["experts_ms_per_rank"],
         "gpu_launches": 6 * args.steps,
-        "clocks": clocks,
+        "clocks": r["clocks"],
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
@@ -635,18 +708,22 @@ def run_ep(args, world, rank, local):
 E2E_CHUNKS = 8  # sequence groups of the cfg4 host pipeline
 
 
-def run_e2e(args, world, rank, local):
-    """--config cfg4: the full CTR model forward (pooling -> RepEncoder ->
-    8 x (attention + MoE) -> MLP head) on one packed batch; metric = ms per
-    batch.  Every rank runs its own replica (the model does not shard)."""
+def measure_e2e_model(args, world, rank, local, flush, steps: int, warmup: int,
+                      sampler=None, cpu_seconds: float = 0.0) -> dict:
+    """Configuration 4: the full CTR model forward (pooling -> RepEncoder ->
+    8 x (attention + MoE) -> MLP head) on one packed batch of 2048 sequences,
+    ms per batch, with inputs resident on the device and end to end from
+    pinned host buffers (CTRModel.predict_host).  Every rank runs its own
+    replica (the model does not shard).  cpu_seconds > 0 also times the
+    oracle on a sample (rank 0)."""
     from cti_b200 import _lib, ops, synth
     from cti_b200.model import build_ctr_model
 
     dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     bb, uo, T = synth.cfg4_batch(seed=rank)
     model = build_ctr_model(bb.vocab.tolist())
     synth.init_ctr_model(model)
+    model.rep_encoder.emb.weight = torch.nn.Parameter(torch.empty(0), requires_grad=False)
     model.to(dev)
     model.rep_encoder.emb.weight = torch.nn.Parameter(
         synth.embedding_table(bb.total_rows, 64, seed=rank, device=dev), requires_grad=False)
@@ -655,18 +732,16 @@ def run_e2e(args, world, rank, local):
             "_val_offsets": bb.val_offsets, "user_offsets": uo}
     batch = {k: v.to(dev) for k, v in host.items()}
     batch["max_seqlen"] = 256
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         model.predict(batch)
     torch.cuda.synchronize(dev)
     _lib.raise_on_status(dev)
-    sampler = ClockSampler(dev) if rank == 0 else None
     barrier(world)
     torch.cuda.synchronize(dev)
     if sampler:
         sampler.start()
-    times = time_steps(lambda: model.predict(batch), args.steps, flush, dev)
+    times = time_steps(lambda: model.predict(batch), steps, flush, dev)
     torch.cuda.synchronize(dev)
     barrier(world)
     clocks = sampler.stop() if sampler else None
@@ -682,11 +757,11 @@ def run_e2e(args, world, rank, local):
     def e2e_step():
         model.predict_host(pinned, chunks=E2E_CHUNKS, out=probs_h)
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         e2e_step()
     barrier(world)
     torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(statistics.median(time_steps(e2e_step, args.steps, flush, dev,
+    e2e_ms = max_over_ranks(statistics.median(time_steps(e2e_step, steps, flush, dev,
                                                          hide_host=False)), world, dev)
 
     # Stage split of one forward (CUDA events), median of 3.
@@ -710,7 +785,7 @@ def run_e2e(args, world, rank, local):
         mark("rep_norm_linear")
         cu = batch["user_offsets"].to(torch.int32)
         h, _ = enc(x, {"cu_seqlens": cu, "max_seqlen": 256, "mark": mark})
-        torch.sigmoid(torch.clamp(model.linear(h), -15, 15).float())
+        model.head(h)
         mark("head")
         torch.cuda.synchronize(dev)
         acc = {k: 0.0 for k in stage}
@@ -738,28 +813,15 @@ def run_e2e(args, world, rank, local):
     N = bb.values.numel()
     pool_bytes = 8 * N + 8 * 28 * (T + 1) + 128 * N + 2 * T * 28 * 64
     pool_gbs = pool_bytes / (stages["pool"] / 1e3) / 1e9
-    if rank != 0:
-        return
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_e2e(model, bb, uo, args.cpu_seconds)
+    if rank == 0 and cpu_seconds > 0:
+        cpu = cpu_baseline_e2e(model, bb, uo, cpu_seconds)
     h2d = sum(v.numel() * v.element_size() for v in host.values())
-    line = {
-        "metric": "e2e_forward_ms_per_batch", "value": step_ms, "unit": "ms/batch",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": f"cfg4: CTR model forward, {synth.CFG4_SAMPLES} packed sequences "
-                               f"U{{16..256}} ({T} tokens), 28 bags per token, RepEncoder "
-                               "LN(1792)+Linear(1792->256), 8 x (varlen causal attention 8x32 + "
-                               "Top-2 MoE 16 experts d_ff 1024), MLP head 256->128->1",
-                   "tokens": T, "ids": N, "layers": 8,
-                   "attention": "cti_varlen_attention (this library)",
-                   "l2": "flushed (256 MiB write) before every timed step",
-                   "per_gpu": "one replica"},
-        "e2e": {"value": e2e_ms, "unit": "ms/batch", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": T * 4, "chunks": E2E_CHUNKS},
-        "roofline": {"bound": "tensor", "kernel": "fused_ffn_kernel<256> (one layer, timed alone)",
+    out = {
+        "ms_per_batch": step_ms, "tokens": T, "ids": N,
+        "e2e_ms_per_batch": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * 4,
+        "chunks": E2E_CHUNKS,
+        "roofline": {"bound": "tensor", "kernel": "fused expert FFN (one layer, timed alone)",
                      "achieved": ffn_tflops, "peak": float(peaks["bf16_tflops"]),
                      "unit": "TFLOP/s", "frac": ffn_tflops / float(peaks["bf16_tflops"]),
                      "peak_source": f"bf16_tflops of {peak_src}", "flops_per_launch": ffn_flops,
@@ -768,11 +830,50 @@ def run_e2e(args, world, rank, local):
                     "bytes_per_launch": pool_bytes,
                     "note": "algorithmic bytes (128 B per id) over time; Zipf ids re-hit rows "
                             "in L2, so this exceeds the HBM copy bandwidth"},
-        "stages_ms": stages,
-        "tokens_per_s": T / (step_ms / 1e3),
-        "gpu_launches": (2 + 7 * enc.num_layers) * args.steps,
-        "clocks": clocks,
-        "cpu_baseline": cpu,
+        "stages_ms": stages, "tokens_per_s": T / (step_ms / 1e3),
+        "launches_per_batch": 2 + 7 * enc.num_layers, "clocks": clocks, "cpu_baseline": cpu,
+    }
+    del model, batch, pinned
+    torch.cuda.empty_cache()
+    return out
+
+
+def cfg4_config(T: int, N: int) -> dict:
+    from cti_b200 import synth
+
+    return {"workload": f"cfg4: CTR model forward, {synth.CFG4_SAMPLES} packed sequences "
+                        f"U{{16..256}} ({T} tokens), 28 bags per token, RepEncoder "
+                        "LN(1792)+Linear(1792->256), 8 x (varlen causal attention 8x32 + "
+                        "Top-2 MoE 16 experts d_ff 1024), MLP head 256->128->1",
+            "tokens": T, "ids": N, "layers": 8,
+            "attention": "cti_varlen_attention (this library)",
+            "l2": "flushed (256 MiB write) before every timed step", "per_gpu": "one replica"}
+
+
+def run_e2e(args, world, rank, local):
+    """--config cfg4: the full CTR model forward alone; metric = ms per batch."""
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    sampler = ClockSampler(dev) if rank == 0 else None
+    r = measure_e2e_model(args, world, rank, local, flush, args.steps, args.warmup, sampler,
+                          cpu_seconds=0.0 if (world > 1 or args.no_cpu_baseline)
+                          else args.cpu_seconds)
+    if rank != 0:
+        return
+    line = {
+        "metric": "e2e_forward_ms_per_batch", "value": r["ms_per_batch"], "unit": "ms/batch",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["ms_per_batch"], "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": cfg4_config(r["tokens"], r["ids"]),
+        "e2e": {"value": r["e2e_ms_per_batch"], "unit": "ms/batch",
+                "h2d_bytes_per_step": r["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": r["d2h_bytes_per_step"], "chunks": r["chunks"]},
+        "roofline": r["roofline"], "pooling": r["pooling"], "stages_ms": r["stages_ms"],
+        "tokens_per_s": r["tokens_per_s"],
+        "gpu_launches": r["launches_per_batch"] * args.steps,
+        "clocks": r["clocks"], "cpu_baseline": r["cpu_baseline"],
     }
     print(json.dumps(line), flush=True)
 
@@ -943,6 +1044,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="leave the cfg5 expert-parallel measurement out of the cfg2 line")
+    ap.add_argument("--no-e2e-model", action="store_true",
+                    help="leave the cfg4 model forward out of the cfg2 line")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--config", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
                     help="cfg2: MoE layer (default, the headline); cfg3: embedding bag; "

@@ -60,6 +60,10 @@ SIGNATURES = {
         _I,
         [_P, _I64, _P, _P, _P, _P, _P, _P, _I, _I, _I64, _I, _I, _I, _P, _P, _P],
     ),
+    "cti_moe_expert_ffn_fused_pair": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _I, _I, _I64, _I, _I, _I, _P, _P, _P],
+    ),
     "cti_moe_expert_ffn_fused_supported": (_I, [_I, _I, _I, _I64]),
     "cti_moe_combine": (_I, [_P, _I64, _P, _P, _I64, _I, _P, _P, _P]),
     "cti_moe_layer_workspace_bytes": (_SZ, [_I64, _I, _I, _I]),

@@ -272,8 +272,197 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
 }
 
 // ---------------------------------------------------------------------------
+// CTA pairs (thread-block clusters of 2): one tcgen05.mma.cta_group::2 covers
+// both SMs of the pair - A is split by rows (each CTA holds its 128 rows in
+// its own shared or tensor memory), B by its N rows (each CTA holds half),
+// D by rows (each CTA's TMEM holds its 128 rows x N).  One thread of the
+// even CTA (the leader) issues the MMAs; barriers that it waits on live in
+// its shared memory, and the odd CTA reaches them through shared::cluster
+// addresses (mapa); a completion meant for both CTAs is committed twice.
+// ---------------------------------------------------------------------------
+CTI_DEVICE uint32_t cluster_cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of the same shared-memory offset in CTA `rank`
+// of this cluster.
+CTI_DEVICE uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// All threads of both CTAs: release this CTA's prior writes, then wait for
+// the peer (barrier.cluster is a hardware barrier with no time limit; both
+// CTAs reach every use of it unconditionally).
+CTI_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Arrives on an mbarrier anywhere in the cluster (release at cluster scope).
+CTI_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+CTI_DEVICE void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
+          cluster_addr),
+      "r"(bytes)
+      : "memory");
+}
+
+CTI_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait with acquire at cluster scope, for barriers that the peer CTA
+// (or MMAs of the pair) arrive on.
+CTI_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int32_t* status, int32_t where,
+                                  volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 63u) == 0u) {
+      if (abort != nullptr && *abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_status(status, CTI_ERR_TIMEOUT, where);
+        if (abort != nullptr) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// TMA 2-D load into this CTA's shared memory whose completion (bytes) is
+// signalled on an mbarrier of either CTA of the pair (the leader's).
+CTI_DEVICE void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t cluster_bar,
+                                 int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Tensor memory of a CTA pair: one warp of each CTA (the same warp index)
+// allocates / frees the same columns in both.
+CTI_DEVICE void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+
+CTI_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+CTI_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Pair MMA, A and B from shared memory.
+CTI_DEVICE void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair MMA, A from tensor memory (each CTA's 128 rows in its own TMEM).
+CTI_DEVICE void umma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at `cluster_addr` (either CTA of the pair)
+// when every pair MMA issued so far by this thread has completed.
+CTI_DEVICE void umma_commit_pair(uint32_t cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_addr)
+      : "memory");
+}
+
+// 32 lanes x 8 consecutive 32-bit columns.
+CTI_DEVICE void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+}
+
+// 32 lanes x 4 consecutive 32-bit columns.
+CTI_DEVICE void tmem_st_32x32b_x4(uint32_t taddr, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+// Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15).
+CTI_DEVICE void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Numerics shared by epilogues.
 // ---------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100): a 64-bit register holds two floats, and the
+// .f32x2 instructions apply the IEEE operation (round to nearest) to each
+// lane independently - two results bit-equal to the scalar ones per issue.
+CTI_DEVICE uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+CTI_DEVICE void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+CTI_DEVICE uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+CTI_DEVICE uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+CTI_DEVICE uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 CTI_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

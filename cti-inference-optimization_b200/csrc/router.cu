@@ -6,20 +6,24 @@
 // with fp32 weights.
 //
 // Summation order (reproduced bit for bit by oracle/router_order.c): every
-// logit is one fused-multiply-add chain over d = 0..D-1 in increasing order,
-// starting from 0, and the bias is added after it.
+// logit is the sum of two fused-multiply-add chains, one over the even d
+// and one over the odd d, each in increasing d starting from 0; then
+// logit = (even + odd) + bias.  The two chains are the two lanes of one
+// packed fma.rn.f32x2: the pair (x[d], x[d+1]) of a token row times the pair
+// (w[d], w[d+1]) of an expert row, both adjacent in memory, so one issue
+// does two FMAs with no data rearranged.
 //
 // The logits of a 128-token block are a [128 x D] x [D x E] fp32 product,
-// computed as a register-tiled SGEMM: each thread owns a 4-token x 4-expert
-// tile (16 independent chains): tokens tg + 32i and experts eg + EG*j, so
-// the 8 (or 2) token rows and 4 (or 16) expert rows a warp reads at once are
-// consecutive rows, which the 16-byte row padding spreads over the banks.  Activations (bf16, [token][d]) and router
-// weights (fp32, [expert][d]) stream through a kStages-deep ring of
-// shared-memory stages, kDC d-values each, filled with cp.async straight
-// from global memory: coalesced row segments, no register staging, and
-// kStages-1 steps of loads in flight while a step is multiplied.  Per 4
-// d-values a thread reads 4 x 8 bytes of activations and 4 x 16 bytes of
-// weights (padded rows, conflict-free) for 64 FMAs.
+// computed as a register-tiled SGEMM: each thread owns TPT tokens x 4
+// experts (tokens tg + TG*i, experts eg + EG*j), each an accumulator pair,
+// so the token rows and expert rows a warp reads at once are consecutive
+// rows, which the 16-byte row padding spreads over the banks.  Activations
+// (bf16, [token][d]) and router weights (fp32, [expert][d]) stream through a
+// kStages-deep ring of shared-memory stages, kDC d-values each, filled with
+// cp.async straight from global memory: coalesced row segments, no register
+// staging, and kStages-1 steps of loads in flight while a step is
+// multiplied.  Per 8 d-values a thread reads TPT x 16 bytes of activations
+// and 4 x 32 bytes of weights for TPT x 4 x 4 packed FMAs.
 //
 // The block also produces the dispatch metadata: for each of its 128 tokens
 // the rank of each route among the block's earlier routes to the same expert
@@ -45,9 +49,20 @@ struct RouterSmem {
   static constexpr size_t kBytes = kMain + (size_t)(1 + kTok / 32) * EMAX * 4;
 };
 
+// Thread tile: TPT tokens x 4 experts.  EG expert groups of 4, TG token
+// groups, NT = TG * EG threads (at least one thread per token of the block).
+template <int EMAX>
+struct RouterTile {
+  static constexpr int EG = EMAX / 4;
+  static constexpr int TPT = EMAX <= 8 ? 2 : (EMAX <= 32 ? 4 : 8);
+  static constexpr int TG = kTok / TPT;
+  static constexpr int NT = TG * EG;
+  static_assert(NT >= kTok && NT <= 512, "router block size");
+};
+
 template <int EMAX>
 constexpr int router_threads() {
-  return 8 * EMAX < kTok ? kTok : 8 * EMAX;
+  return RouterTile<EMAX>::NT;
 }
 
 // 16-byte global -> shared copy; src_bytes = 0 fills the destination with zeros.
@@ -72,9 +87,11 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
   // complete before it reads the histograms.
   grid_dependents_launch();
   using SM = RouterSmem<EMAX>;
-  constexpr int EG = EMAX / 4;       // expert groups of 4
-  constexpr int NG = 32 * EG;        // GEMM threads: 32 token groups x EG expert groups
-  constexpr int NT = NG < kTok ? kTok : NG;  // at least one thread per token
+  using TL = RouterTile<EMAX>;
+  constexpr int EG = TL::EG;
+  constexpr int TG = TL::TG;
+  constexpr int TPT = TL::TPT;
+  constexpr int NT = TL::NT;
   // Dynamic shared memory: the stage ring while the logits are accumulated,
   // then reused as lg[kTok][EMAX + 1]; then cnt[EMAX] (block counts) and the
   // per-warp counts [kTok/32][EMAX].
@@ -84,15 +101,14 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
 
   const int tid = threadIdx.x;
   const int eg = tid % EG;   // experts eg + EG*j, j = 0..3
-  const int tg = tid / EG;   // tokens  tg + 32*i, i = 0..3
-  const bool gemm = tid < NG;
+  const int tg = tid / EG;   // tokens  tg + TG*i, i = 0..TPT-1
   const int64_t t0 = (int64_t)blockIdx.x * kTok;
 
-  float acc[4][4];
+  uint64_t acc[TPT][4];  // (even-d chain, odd-d chain) per token and expert
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < TPT; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;  // both lanes +0.0f
 
   // Stage s of the ring: x part [kTok][kXPitch] bytes, then w part
   // [EMAX][kWPitch] bytes.  Step k covers d in [k*kDC, k*kDC + kDC).
@@ -131,46 +147,52 @@ __global__ void __launch_bounds__(router_threads<EMAX>()) router_kernel(
     __syncthreads();  // step k has landed for all threads; step k-1's slot is free
     if (k + kStages - 1 < nsteps) issue(k + kStages - 1);
     cp_async_commit();
-    if (gemm) {
+    {
       const int dc = min(kDC, D - k * kDC);
       const uint8_t* xs = x_stage(k % kStages) + tg * kXPitch;
       const uint8_t* ws = w_stage(k % kStages) + eg * kWPitch;
-#pragma unroll 2
-      for (int d4 = 0; d4 < dc / 4; ++d4) {
-        float xv[4][4], wv[4][4];
+      // Two steps in flight give the next step's loads cover; at EMAX 128
+      // (512 threads, 128 registers each) one step keeps the tile in registers.
+#pragma unroll(EMAX >= 128 ? 1 : 2)
+      for (int d8 = 0; d8 < dc / 8; ++d8) {
+        uint64_t xp[TPT][4], wp[4][4];  // (d + 2q, d + 2q + 1) pairs, q = 0..3
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(xs + i * 32 * kXPitch + d4 * 8);
-          xv[i][0] = __uint_as_float(raw.x << 16);
-          xv[i][1] = __uint_as_float(raw.x & 0xffff0000u);
-          xv[i][2] = __uint_as_float(raw.y << 16);
-          xv[i][3] = __uint_as_float(raw.y & 0xffff0000u);
+        for (int i = 0; i < TPT; ++i) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(xs + i * TG * kXPitch + d8 * 16);
+          const uint32_t w32[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            xp[i][q] = f2_pack(__uint_as_float(w32[q] << 16),
+                               __uint_as_float(w32[q] & 0xffff0000u));
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float4 q = *reinterpret_cast<const float4*>(ws + j * EG * kWPitch + d4 * 16);
-          wv[j][0] = q.x;
-          wv[j][1] = q.y;
-          wv[j][2] = q.z;
-          wv[j][3] = q.w;
+          const float4* wr = reinterpret_cast<const float4*>(ws + j * EG * kWPitch + d8 * 32);
+          const float4 a = wr[0], b = wr[1];
+          wp[j][0] = f2_pack(a.x, a.y);
+          wp[j][1] = f2_pack(a.z, a.w);
+          wp[j][2] = f2_pack(b.x, b.y);
+          wp[j][3] = f2_pack(b.z, b.w);
         }
 #pragma unroll
-        for (int dd = 0; dd < 4; ++dd)
+        for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < TPT; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i][dd], wv[j][dd], acc[i][j]);
+            for (int j = 0; j < 4; ++j) acc[i][j] = f2_fma(xp[i][q], wp[j][q], acc[i][j]);
       }
     }
   }
   cp_async_wait<0>();
   __syncthreads();  // xs/ws are about to be overwritten by lg
-  if (gemm) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < TPT; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) lg[tg + 32 * i][eg + EG * j] = acc[i][j];
-  }
+    for (int j = 0; j < 4; ++j) {
+      float even, odd;
+      f2_unpack(acc[i][j], even, odd);
+      lg[tg + TG * i][eg + EG * j] = even + odd;
+    }
   __syncthreads();
 
   // One thread per token: logits, top-2 by a strict '>' scan in expert order

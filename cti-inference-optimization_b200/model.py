@@ -220,8 +220,11 @@ class CTRModel(nn.Module):
         cu, max_len = self.sequence_info(batch, dev)
         x = self.rep_encoder(batch)
         h, _ = self.seq_encoder(x, {"cu_seqlens": cu, "max_seqlen": max_len})
-        logits = torch.clamp(self.linear(h), min=-15.0, max=15.0)
-        return logits, None
+        return self.head(h), None
+
+    def head(self, h: torch.Tensor) -> torch.Tensor:
+        """Logits [T, 1]: the MLP head, clamped to +-15 (baseline/infer.py:437)."""
+        return torch.clamp(self.linear(h), min=-15.0, max=15.0)
 
     @torch.no_grad()
     def predict(self, batch: dict) -> torch.Tensor:

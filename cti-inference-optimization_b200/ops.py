@@ -120,8 +120,10 @@ def expert_ffn_fused(
     group_offsets: torch.Tensor,
     act: str = "gelu",
     out: torch.Tensor | None = None,
+    pair: bool = False,
 ) -> torch.Tensor:
-    """Stage 3, fused: Y = act(Xp @ W1[e]^T + b1[e]) @ W2[e]^T + b2[e] per group."""
+    """Stage 3, fused: Y = act(Xp @ W1[e]^T + b1[e]) @ W2[e]^T + b2[e] per group.
+    ``pair``: the CTA-pair kernel (cti_moe_expert_ffn_fused_pair, d_model 256)."""
     require_cuda(xp, "Xp", torch.bfloat16)
     require_cuda(w1, "W1", torch.bfloat16)
     require_cuda(w2, "W2", torch.bfloat16)
@@ -133,12 +135,13 @@ def expert_ffn_fused(
     dev = xp.device
     if out is None:
         out = torch.empty((rows, D), dtype=torch.bfloat16, device=dev)
+    fn = lib.cti_moe_expert_ffn_fused_pair if pair else lib.cti_moe_expert_ffn_fused
     check(
-        lib.cti_moe_expert_ffn_fused(
+        fn(
             ptr(xp), ptr(w1), ptr(b1), ptr(w2), ptr(b2), ptr(group_offsets), G, Gw, rows, D, F,
             _lib.ACTIVATIONS[act], ptr(out), ptr(status_word(dev)), stream_handle(dev),
         ),
-        "cti_moe_expert_ffn_fused",
+        "cti_moe_expert_ffn_fused_pair" if pair else "cti_moe_expert_ffn_fused",
     )
     return out
 

@@ -185,6 +185,18 @@ int cti_moe_expert_ffn_fused_gather(const void* x_bf16, int64_t T, const int32_t
                                     int64_t rows_total, int D, int F, int act, void* Y_bf16,
                                     int32_t* status, void* stream);
 
+/* The same on CTA pairs (thread-block clusters of two SMs, one
+ * tcgen05.mma.cta_group::2 stream per pair, 256-row tiles): each SM holds
+ * half of every weight chunk, so it streams half the weight bytes per FLOP,
+ * and the weight slots are double-buffered.  D == 256 only; otherwise the
+ * same arguments, shapes and results (within fp32 accumulation order:
+ * every row's result is computed the same way, bit for bit). */
+int cti_moe_expert_ffn_fused_pair(const void* Xp_bf16, const void* W1_bf16, const float* b1,
+                                  const void* W2_bf16, const float* b2,
+                                  const int32_t* group_offsets, int G, int Gw,
+                                  int64_t rows_total, int D, int F, int act, void* Y_bf16,
+                                  int32_t* status, void* stream);
+
 /* 1 if the fused kernels take this shape (D in {128, 256}, F % 128 == 0,
  * F <= 1024, G <= 256 groups, rows_total < 2^31 - 256), else 0. */
 int cti_moe_expert_ffn_fused_supported(int D, int F, int G, int64_t rows_total);

@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 
 from .embbag_ref import embbag_ref
-from .moe_ref import smoe_ref
+from .moe_ref import gate_ref, logits_fp64, smoe_ref
 
 
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -46,9 +46,16 @@ def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def ctr_forward_ref(sd: dict, batch: dict, *, slot_num: int, n_heads: int, num_layers: int,
-                    num_experts: int, table_row_base=None, vocab=None):
+                    num_experts: int, table_row_base=None, vocab=None, force_routes=None,
+                    routing: list | None = None):
     """Returns (encoder output [T, D], clamped logits [T], probabilities [T]),
-    all fp32.  ``sd`` maps reference parameter names to tensors."""
+    all fp32.  ``sd`` maps reference parameter names to tensors.
+
+    ``force_routes[i]`` ([T, 2]), when given, fixes layer i's top-2 experts
+    (see moe_ref.gate_ref).  ``routing``, when a list, receives per layer
+    (the gate's own top-2 [T, 2] on this run's activations, the fp64 gap
+    [T] between its top-1/top-2 or top-2/top-3 logits, whichever is
+    smaller)."""
     # The embedding table stays in its own dtype: the pooling upcasts only
     # the rows it gathers.
     g = {k: v.float() for k, v in sd.items() if k != "rep_encoder.emb.weight"}
@@ -76,8 +83,14 @@ def ctr_forward_ref(sd: dict, batch: dict, *, slot_num: int, n_heads: int, num_l
         b1 = torch.stack([g[m + f"experts.{e}.fc1.bias"] for e in range(num_experts)])
         w2 = torch.stack([g[m + f"experts.{e}.fc2.weight"] for e in range(num_experts)])
         b2 = torch.stack([g[m + f"experts.{e}.fc2.bias"] for e in range(num_experts)])
-        y, _ = smoe_ref(h, g[m + "gate.w_g.weight"], g[m + "gate.w_g.bias"], w1, b1, w2, b2,
-                        act="gelu", renorm=True)
+        wg, bg = g[m + "gate.w_g.weight"], g[m + "gate.w_g.bias"]
+        if routing is not None:
+            own = gate_ref(h, wg, bg).idx
+            s_ = logits_fp64(h, wg, bg).sort(dim=-1, descending=True).values
+            gap = torch.minimum(s_[:, 0] - s_[:, 1], s_[:, 1] - s_[:, 2])
+            routing.append((own, gap))
+        y, _ = smoe_ref(h, wg, bg, w1, b1, w2, b2, act="gelu", renorm=True,
+                        force_idx=None if force_routes is None else force_routes[i])
         x = x + y
     z = F.relu(F.linear(x, g["linear.0.weight"], g["linear.0.bias"]))
     logits = torch.clamp(F.linear(z, g["linear.2.weight"], g["linear.2.bias"]), -15.0, 15.0)

@@ -27,11 +27,17 @@ class GateRef:
 
 
 def gate_ref(x: torch.Tensor, wg: torch.Tensor, bg: torch.Tensor, renorm: bool = True,
-             tie_lower_id: bool = True) -> GateRef:
-    """baseline/infer.py:298-309 (eval mode: no gating noise)."""
+             tie_lower_id: bool = True, force_idx: torch.Tensor | None = None) -> GateRef:
+    """baseline/infer.py:298-309 (eval mode: no gating noise).  With
+    `force_idx` [T, 2] the top-2 experts are taken from it instead of chosen
+    (the scores are still this gate's probabilities of those experts): the
+    end-to-end check runs the oracle on the routes the device chose."""
     logits = F.linear(x.float(), wg.float(), bg.float())
     probs = torch.softmax(logits, dim=-1)
-    if tie_lower_id:
+    if force_idx is not None:
+        order = force_idx.long()
+        score = probs.gather(-1, order)
+    elif tie_lower_id:
         order = torch.sort(probs, dim=-1, descending=True, stable=True).indices[..., :2]
         score = probs.gather(-1, order)
     else:
@@ -49,11 +55,11 @@ def expert_ref(x: torch.Tensor, w1, b1, w2, b2, act: str) -> torch.Tensor:
 
 
 def smoe_ref(x: torch.Tensor, wg, bg, w1, b1, w2, b2, act: str = "gelu", renorm: bool = True,
-             tie_lower_id: bool = True):
+             tie_lower_id: bool = True, force_idx: torch.Tensor | None = None):
     """baseline/infer.py:323-353.  x [T, D]; w1 [E, F, D]; w2 [E, D, F] (all cast
-    to fp32).  Returns (out [T, D] fp32, GateRef)."""
+    to fp32).  Returns (out [T, D] fp32, GateRef).  `force_idx`: see gate_ref."""
     x = x.float()
-    g = gate_ref(x, wg, bg, renorm, tie_lower_id)
+    g = gate_ref(x, wg, bg, renorm, tie_lower_id, force_idx)
     out = torch.zeros_like(x)
     E = wg.shape[0]
     for e in range(E):

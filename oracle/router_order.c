@@ -4,9 +4,11 @@
  * Same arithmetic as TopKGate.forward (baseline/infer.py:298-309) -
  * logits = x . w_g^T + b, top-2, softmax scores - but with the summation
  * order of the sm_100a kernel made explicit so expert indices can be
- * compared bit for bit: every logit is one fused-multiply-add chain over
- * d = 0..D-1 in increasing order starting from 0.0f, and the bias is added
- * in a separate rounding.
+ * compared bit for bit: every logit is the sum of two fused-multiply-add
+ * chains, one over the even d = 0, 2, 4, ... and one over the odd
+ * d = 1, 3, 5, ..., each in increasing order starting from 0.0f; then
+ * logit = (even + odd) + bias, two more roundings.  (The kernel runs the
+ * two chains as the two lanes of one packed fp32x2 FMA.)  D is even.
  * Top-2 scans experts in order with strict '>' (the lower id wins a tie,
  * as in fused_top2_gate_kernel, online_best/infer.py:1710-1757).
  * renorm=1 -> gates p1/(p1+p2), p2/(p1+p2); renorm=0 -> raw softmax p1, p2.
@@ -29,9 +31,12 @@ void router_order_ref(const uint16_t* x, const float* wg, const float* bg, int64
     const uint16_t* xr = x + t * D;
     for (int e = 0; e < E; ++e) {
       const float* w = wg + (int64_t)e * D;
-      float acc = 0.0f;
-      for (int d = 0; d < D; ++d) acc = fmaf(bf16_to_f32(xr[d]), w[d], acc);
-      l[e] = acc + bg[e];
+      float even = 0.0f, odd = 0.0f;
+      for (int d = 0; d < D; d += 2) {
+        even = fmaf(bf16_to_f32(xr[d]), w[d], even);
+        odd = fmaf(bf16_to_f32(xr[d + 1]), w[d + 1], odd);
+      }
+      l[e] = (even + odd) + bg[e];
       if (logits_out) logits_out[t * E + e] = l[e];
     }
     float b1 = l[0], b2 = 0.0f;

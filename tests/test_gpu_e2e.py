@@ -174,9 +174,24 @@ def test_predict_host_chunks_match_predict(cuda_device):
 def test_full_cfg4_model_matches_oracle_on_sampled_sequences(cuda_device):
     """The whole configuration-4 forward: 2048 packed sequences (284,237
     tokens, 204 M ids), 8 layers, per-slot fp16 tables, run on the device
-    as the benchmark runs it.  Sequences are independent, so the oracle
-    runs on 24 seeded sampled sequences alone (their flat-layout sub-batch)
-    and their probabilities must agree within 1e-3 absolute."""
+    as the benchmark runs it.  Sequences are independent, so the oracle runs
+    on 24 seeded sampled sequences alone (their flat-layout sub-batch).
+
+    The model's activations are bf16, so its router sees bf16 LayerNorm
+    outputs, and a token whose top-2 logits are nearly tied (fp64 gap of a
+    few 1e-3) can take a different second expert at some layer - the
+    reference's own bf16 model (online_best casts everything but nothing
+    else to bf16) does the same.  So the check is in two parts:
+      * the oracle follows the device's routes at every layer (the experts
+        the device chose; the oracle's own fp32 gate probabilities weight
+        them): every probability within 1e-3 absolute, the north-star bound;
+      * every route where the device differs from the oracle's own top-2
+        lies in the fp64 near-tie band (gap below 1e-2, about 3 % of the
+        logits' spread of 0.3; flips were measured at gaps up to 5.6e-3),
+        and such routes are few (at most 3 % of token-layers; a CPU
+        emulation of the bf16 rounding points gives about 1.3 %).
+    Unforced, the largest difference is printed (about 1e-3, at a token
+    whose layer-0 routing flips at a gap of 6e-4)."""
     from cti_b200 import _lib, synth
     from cti_b200.model import build_ctr_model
 
@@ -196,18 +211,36 @@ def test_full_cfg4_model_matches_oracle_on_sampled_sequences(cuda_device):
     model.prepare_for_inference()
     batch = {"_flat_values": bb.values, "_flat_row_offsets": bb.row_offsets,
              "_val_offsets": bb.val_offsets, "user_offsets": uo}
-    probs = model.predict({k: v.to(cuda_device) for k, v in batch.items()}).cpu()
-    _lib.raise_on_status(cuda_device)
-    assert probs.shape == (T,) and torch.isfinite(probs).all()
-
     seqs = sorted(torch.randperm(synth.CFG4_SAMPLES,
                                  generator=torch.Generator().manual_seed(7))[:24].tolist())
+    rows = torch.cat([torch.arange(int(uo[s]), int(uo[s + 1])) for s in seqs])
+    # Each MoE layer's routes on the device (its gate on the layer's input).
+    routes = []
+    hooks = [m.register_forward_hook(
+        lambda mod, inp, out: routes.append(mod.gate(inp[0])[0].reshape(-1, 2)[
+            rows.to(cuda_device)].cpu())) for m in model.seq_encoder.moe]
+    probs = model.predict({k: v.to(cuda_device) for k, v in batch.items()}).cpu()
+    for h in hooks:
+        h.remove()
+    _lib.raise_on_status(cuda_device)
+    assert probs.shape == (T,) and torch.isfinite(probs).all() and len(routes) == 8
+
     sub = synth.sequence_subbatch(bb, uo, seqs)
     sd["rep_encoder.emb.weight"] = table
     torch.set_num_threads(8)
-    _, _, ref = e2e_ref.ctr_forward_ref(sd, sub, slot_num=28, n_heads=8, num_layers=8,
-                                        num_experts=16, table_row_base=bb.table_row_base,
-                                        vocab=bb.vocab)
-    mine = torch.cat([probs[int(uo[s]):int(uo[s + 1])] for s in seqs])
+    kw = dict(slot_num=28, n_heads=8, num_layers=8, num_experts=16,
+              table_row_base=bb.table_row_base, vocab=bb.vocab)
+    mine = probs[rows]
+    _, _, free = e2e_ref.ctr_forward_ref(sd, sub, **kw)
+    print(f"unforced: max |p - p_ref| {float((mine - free).abs().max()):.2e}")
+    routing = []
+    _, _, ref = e2e_ref.ctr_forward_ref(sd, sub, force_routes=routes, routing=routing, **kw)
     assert mine.numel() == ref.numel() == int(sub["user_offsets"][-1])
     np.testing.assert_allclose(mine.numpy(), ref.numpy(), rtol=0, atol=1e-3)
+    flips = 0
+    for layer, ((own, gap), dev_idx) in enumerate(zip(routing, routes)):
+        differ = (own != dev_idx.long()).any(dim=1)
+        assert (gap[differ] < 1e-2).all(), (layer, gap[differ].max())
+        flips += int(differ.sum())
+    print(f"routes differing from the oracle's own top-2: {flips} of {8 * mine.numel()}")
+    assert flips <= 0.03 * 8 * mine.numel()

@@ -159,3 +159,67 @@ def test_layer_matches_staged_fused_and_support_query(cuda_device):
     staged = m.forward_staged(x, fused=True)["out"]
     _lib.raise_on_status(cuda_device)
     assert torch.equal(out, staged)
+
+
+# The CTA-pair kernel (d_model 256): 256-row tiles whose odd CTA may hold no
+# rows (groups of <= 128 rows), single rows, empty groups, up to 256 groups.
+PAIR_CASES = [
+    (1024, [256], 1, "gelu"),
+    (128, [1], 1, "gelu"),
+    (1024, [300, 0, 1000, 17, 128, 129, 5000, 2, 900, 0, 0, 33, 64, 65, 700, 1], 16, "gelu"),
+    (512, [640, 640, 384, 100, 129], 5, "relu"),
+    (1024, [40000, 30000, 20000, 10000], 4, "gelu"),
+    (256, [3, 250, 0, 257, 511, 1] * 40, 7, "none"),
+]
+
+
+@pytest.mark.parametrize("Fd,sizes,Gw,act", PAIR_CASES)
+def test_fused_ffn_pair_matches_fp32_and_single_cta(cuda_device, Fd, sizes, Gw, act):
+    """cti_moe_expert_ffn_fused_pair against the fp32 reference (max rel err
+    1e-2) and against the one-CTA kernel on the same rows: every row is
+    computed with the same K order and the same bf16 rounding of the hidden
+    activation, so the two agree to fp32 accumulation noise (1e-3)."""
+    from cti_b200 import _lib, ops
+
+    D = 256
+    rows = sum(sizes)
+    g = torch.Generator().manual_seed(rows + Fd + len(sizes))
+    x = torch.randn(rows, D, generator=g).bfloat16()
+    w1 = (torch.randn(Gw, Fd, D, generator=g) * 0.05).bfloat16()
+    b1 = torch.randn(Gw, Fd, generator=g) * 0.1
+    w2 = (torch.randn(Gw, D, Fd, generator=g) * 0.05).bfloat16()
+    b2 = torch.randn(Gw, D, generator=g) * 0.1
+    offs = torch.zeros(len(sizes) + 1, dtype=torch.int32)
+    offs[1:] = torch.cumsum(torch.tensor(sizes), 0)
+    dev = cuda_device
+    args = (x.to(dev), w1.to(dev), b1.to(dev), w2.to(dev), b2.to(dev), offs.to(dev))
+    y_pair = ops.expert_ffn_fused(*args, act=act, pair=True)
+    y_one = ops.expert_ffn_fused(*args, act=act)
+    _lib.raise_on_status(dev)
+    assert max_rel_err(y_pair, y_one.float()) < 1e-3
+    ref = ref_ffn(x, w1, b1, w2, b2, offs, act, Gw)
+    err = max_rel_err(y_pair, ref)
+    assert err < TOL, f"max rel err {err}"
+
+
+def test_fused_ffn_pair_leaves_rows_outside_groups_untouched(cuda_device):
+    """Rows past the last group offset are neither read into results nor
+    written; rows of a pair tile that belong to no group stay as they were."""
+    from cti_b200 import _lib, ops
+
+    dev = cuda_device
+    rows, D, Fd = 700, 256, 256
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(rows, D, generator=g, device=dev).bfloat16()
+    w1 = (torch.randn(1, Fd, D, generator=g, device=dev) * 0.05).bfloat16()
+    b1 = torch.zeros(1, Fd, device=dev)
+    w2 = (torch.randn(1, D, Fd, generator=g, device=dev) * 0.05).bfloat16()
+    b2 = torch.zeros(1, D, device=dev)
+    offs = torch.tensor([0, 300], dtype=torch.int32, device=dev)
+    y = torch.full((rows, D), 7.0, device=dev).bfloat16()
+    ops.expert_ffn_fused(x, w1, b1, w2, b2, offs, out=y, pair=True)
+    _lib.raise_on_status(dev)
+    assert (y[300:] == 7.0).all()
+    ref = ref_ffn(x[:300].cpu(), w1.cpu(), b1.cpu(), w2.cpu(), b2.cpu(),
+                  torch.tensor([0, 300]), "gelu", 1)
+    assert max_rel_err(y[:300], ref) < TOL

@@ -12,7 +12,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("rows,cols", [(1, 256), (7, 256), (4099, 256), (513, 1792), (64, 2048),
-                                       (300, 512), (0, 256)])
+                                       (300, 512), (0, 256), (1000, 128), (77, 200), (33, 8),
+                                       (129, 1800), (65, 264)])
 @pytest.mark.parametrize("with_residual", [True, False])
 def test_add_layernorm_matches_torch(cuda_device, rows, cols, with_residual):
     from cti_b200 import ops
@@ -36,9 +37,11 @@ def test_add_layernorm_matches_torch(cuda_device, rows, cols, with_residual):
 def test_add_layernorm_rejects_bad_shapes(cuda_device):
     from cti_b200 import _lib, ops
 
-    x = torch.zeros(4, 200, dtype=torch.bfloat16, device=cuda_device)
-    w = torch.ones(200, dtype=torch.bfloat16, device=cuda_device)
-    with pytest.raises(RuntimeError):
-        ops.add_layernorm(x, None, w, w)
+    # widths must be multiples of 8 (whole 16-byte vectors), at most 2048
+    for cols in (100, 2056):
+        x = torch.zeros(4, cols, dtype=torch.bfloat16, device=cuda_device)
+        w = torch.ones(cols, dtype=torch.bfloat16, device=cuda_device)
+        with pytest.raises(RuntimeError):
+            ops.add_layernorm(x, None, w, w)
     assert _lib.lib.cti_add_layernorm(None, None, None, None, 4, 256, 1e-5, None, None,
                                       None) == _lib.CTI_ERR_INVALID_ARG
