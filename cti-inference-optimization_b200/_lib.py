@@ -81,6 +81,7 @@ SIGNATURES = {
         [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _P, _I, _P, _P],
     ),
     "cti_selftest_wait_timeout": (_I, [_P, _I64, _P]),
+    "cti_ctr_head": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, ctypes.c_float, _P, _P, _P, _P]),
     "cti_varlen_attention": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _I, _I, _I, _I, _P, _P]),
     "cti_add_layernorm": (
         _I,

@@ -15,20 +15,22 @@
 //             same TMEM columns (two bf16 per 32-bit column)
 //   GEMM2(c): acc2 (TMEM, D cols) += H(c) @ W2[e][:, c*128:+128]^T, with the
 //             A operand read from tensor memory
-// The MMA thread issues GEMM2(c) right after GEMM1(c+1), and GEMM1(c+2) - which
-// overwrites acc1[c%2] - after GEMM2(c): tcgen05.mma instructions of one thread
-// execute in issue order, so GEMM2(c) has read H(c) before GEMM1(c+2) writes
-// there, and the hidden tile never touches shared memory.  While the epilogue
-// turns chunk c into H(c), the tensor core runs GEMM2(c-1) and GEMM1(c+1).
-// After the last chunk, acc2 + b2 is written to Y as bf16.
+// GEMM1s and GEMM2s are issued by two threads of their own.  GEMM1(c+2)
+// overwrites acc1[c%2], so its thread waits until GEMM2(c) - which read H(c)
+// there - has completed (acc1_free[c%2], committed by the GEMM2 thread), and
+// the hidden tile never touches shared memory.  While the epilogue turns
+// chunk c into H(c), the tensor core runs GEMM1(c+1) and GEMM2(c-1); each
+// issuer's barrier waits overlap the other's MMAs (one thread issuing both
+// left the tensor core idle during every wait: the issue queue holds only a
+// few MMAs).  After the last chunk, acc2 + b2 is written to Y as bf16.
 //
-// Roles (576 threads; 608 with the row gather below): warp 0 TMA producer
-// (X tile once per tile unless warp 18 gathers it; W1 and W2 chunks through
-// two rings of whole-chunk slots), warp 1 TMEM owner and MMA issuer
-// (tcgen05.mma M=128, K=16, bf16 -> fp32; N=128 for GEMM1, N=D for GEMM2),
-// warps 2-17 epilogue (four warps per TMEM lane quadrant, each owning 32 of
-// a chunk's 128 columns and a quarter of the output columns; the expert's
-// biases are staged in shared memory once per expert change).
+// Roles (608 threads; 640 with the row gather below): warp 0 TMA producer
+// (X tile once per tile unless warp 19 gathers it; W1 and W2 chunks through
+// two rings of whole-chunk slots), warp 1 TMEM owner and GEMM1 issuer
+// (tcgen05.mma M=128, N=128, K=16, bf16 -> fp32), warps 2-17 epilogue (four
+// warps per TMEM lane quadrant, each owning 32 of a chunk's 128 columns and
+// a quarter of the output columns; the expert's biases are staged in shared
+// memory once per expert change), warp 18 GEMM2 issuer (N=D, A from TMEM).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
 // The epilogue produces H(c) in two halves (chunk columns [0, 64) and
@@ -54,37 +56,37 @@ constexpr int kFC = 128;           // d_ff chunk
 constexpr int kBK = 64;            // bf16 elements per 128-byte swizzled row
 constexpr int kSlab = kBM * kBK * 2;  // 16 KB: one 128x64 bf16 tile
 constexpr int kEpiWarps = 16;
-constexpr int kMaxF = 1024;  // b1 of one expert staged in shared memory
-using Sched = GroupSchedT<256>;
+constexpr int kMaxF = 1024;
+// 128 groups (the library's expert limit) keeps the scheduler's table small
+// enough for the weight rings below.
+using Sched = GroupSchedT<128>;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = 64 + kEpiThreads;
+// warps: 0 W1 / X producer, 1 GEMM1 issuer + TMEM owner, 2-17 epilogue,
+// 18 GEMM2 issuer, 19 W2 producer (20 row gather in the gather variant)
+constexpr int kIssue2Warp = 2 + kEpiWarps;
+constexpr int kProd2Warp = 3 + kEpiWarps;
+constexpr int kGatherWarp = 4 + kEpiWarps;
+constexpr int kThreads = 128 + kEpiThreads;
 constexpr uint32_t kAcc1Col = 256;
-// GEMM2 of chunk c is issued after GEMM1 of chunk c+kLag.  H(c) lives in
-// acc1[c%2], so kLag must be 1: GEMM1(c+2) reuses that buffer.
-constexpr int kLag = 1;
+constexpr int kW1Slots = 3;        // W1 half-chunk slots
+constexpr int kW2Slots = 2;        // W2 half-chunk slots
 
-// Weights stream through two rings of slots, one for W1 chunks ([128 x D])
-// and one for W2 chunks ([D x 128]).  A slot holds one whole chunk and has
-// ONE full barrier, so the MMA thread tests a barrier once per GEMM: on
-// sm_100 every mbarrier test on the MMA-issuing thread costs ~200 cycles of
-// MMA issue, more than the slack of a burst of N=128 MMAs (~14 cycles each
-// above the ~50-cycle issue interval), while commits are cheap (~12).  Each
-// slot has two empty barriers, one per half (the MMA commits after each
-// half), so the producer refills the first half while the tensor core still
-// reads the second.
+// Weights stream through two rings of half-chunk slots, filled by a
+// producer warp each: W1 halves ([128 x D/2], the first or second half of a
+// chunk's K) and W2 halves ([D x 64]).  A chunk's weights can be reloaded
+// only after the MMAs reading the previous contents of their slot have
+// completed, and a reload from L2 takes 1.5-2.3 K cycles; with three W1 and
+// two W2 half slots a reload has 1.5-2 K cycles of other MMAs to hide
+// behind (with one whole-chunk slot per ring it had 1 K and set the pace).
 template <int D>
 struct FF {
-  static constexpr int XK = D / kBK;          // X k-slabs
-  static constexpr int W1H = XK / 2;          // W1 k-slabs [128 x 64] per half slot
-  static constexpr size_t W1C = (size_t)kFC * D * 2;  // bytes of one W1 chunk
-  static constexpr size_t W2H = (size_t)D * kBK * 2;  // one W2 k-slab [D x 64] = half a chunk
-  static constexpr size_t W2C = 2 * W2H;
-  static constexpr int NSLOT = D == 256 ? 1 : 2;      // slots per ring
+  static constexpr int XK = D / kBK;                     // X k-slabs
+  static constexpr int W1HS = XK / 2;                    // W1 k-slabs [128 x 64] per half
+  static constexpr size_t W1H = (size_t)W1HS * kSlab;    // bytes of a W1 half
+  static constexpr size_t W2H = (size_t)D * kBK * 2;     // bytes of a W2 half [D x 64]
   static constexpr size_t X_BYTES = (size_t)XK * kSlab;
-  static constexpr size_t RING_BYTES = (size_t)NSLOT * (W1C + W2C);
-  static constexpr size_t BIAS_BYTES = (size_t)(kMaxF + D) * 4;
-  static constexpr size_t SMEM =
-      1024 + X_BYTES + RING_BYTES + BIAS_BYTES + Sched::smem_bytes() + 256;
+  static constexpr size_t RING_BYTES = kW1Slots * W1H + kW2Slots * W2H;
+  static constexpr size_t SMEM = 1024 + X_BYTES + RING_BYTES + Sched::smem_bytes() + 512;
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
@@ -119,6 +121,18 @@ CTI_DEVICE void prefetch_row_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// A ring position: slot and the parity of its current use.
+struct RingPos {
+  int slot = 0;
+  uint32_t phase = 0;
+  CTI_DEVICE void next(int slots) {
+    if (++slot == slots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 template <int D, bool GATHER>
 __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
     fused_ffn_kernel(const __grid_constant__ CUtensorMap tmX,
@@ -134,27 +148,23 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sx = smem;
-  uint8_t* ring = sx + P::X_BYTES;
-  uint8_t* ring1 = ring;                          // W1 slots
-  uint8_t* ring2 = ring + P::NSLOT * P::W1C;      // W2 slots
-  float* b1s = reinterpret_cast<float*>(ring + P::RING_BYTES);
-  float* b2s = b1s + kMaxF;
-  uint8_t* sched_mem = reinterpret_cast<uint8_t*>(b2s + D);
+  uint8_t* ring1 = sx + P::X_BYTES;                   // W1 half slots
+  uint8_t* ring2 = ring1 + kW1Slots * P::W1H;         // W2 half slots
+  uint8_t* sched_mem = ring2 + kW2Slots * P::W2H;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + Sched::smem_bytes());
-  uint64_t* full1 = bars;                // [NSLOT] W1 chunk landed
-  uint64_t* empty1 = full1 + P::NSLOT;   // [NSLOT][2] W1 half read by the MMAs
-  uint64_t* full2 = empty1 + 2 * P::NSLOT;
-  uint64_t* empty2 = full2 + P::NSLOT;
-  uint64_t* x_full = empty2 + 2 * P::NSLOT;
+  uint64_t* full1 = bars;                  // [kW1Slots]
+  uint64_t* empty1 = full1 + kW1Slots;     // [kW1Slots]
+  uint64_t* full2 = empty1 + kW1Slots;     // [kW2Slots]
+  uint64_t* empty2 = full2 + kW2Slots;     // [kW2Slots]
+  uint64_t* x_full = empty2 + kW2Slots;
   uint64_t* x_empty = x_full + 1;
-  uint64_t* a1_full = x_empty + 1;  // [2] GEMM1(c) done -> epilogue
-  uint64_t* h_full = a1_full + 2;    // [2][2] half h of H(c) written -> MMA
-  uint64_t* a2_full = h_full + 4;
+  uint64_t* a1_full = x_empty + 1;   // [2] GEMM1(c) done -> epilogue
+  uint64_t* h_full = a1_full + 2;    // [2][2] half h of H(c) written -> GEMM2 issuer
+  uint64_t* acc1_free = h_full + 4;  // [2] GEMM2 has read H from acc1[b]
+  uint64_t* a2_full = acc1_free + 2;
   uint64_t* a2_empty = a2_full + 1;
-  uint64_t* drain = a2_empty + 1;
-  uint64_t* bfree = drain + 1;   // epilogue threads done with the staged biases
-  uint64_t* bready = bfree + 1;  // new biases staged
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bready + 1);
+  uint64_t* drain = a2_empty + 1;    // [2] one per issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -162,23 +172,24 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
   const int nch = F / kFC;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P::NSLOT; ++s) {
+    for (int s = 0; s < kW1Slots; ++s) {
       mbar_init(&full1[s], 1);
+      mbar_init(&empty1[s], 1);
+    }
+    for (int s = 0; s < kW2Slots; ++s) {
       mbar_init(&full2[s], 1);
-      for (int h = 0; h < 2; ++h) {
-        mbar_init(&empty1[2 * s + h], 1);
-        mbar_init(&empty2[2 * s + h], 1);
-      }
+      mbar_init(&empty2[s], 1);
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 1);
-    for (int i = 0; i < 2; ++i) mbar_init(&a1_full[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a1_full[i], 1);
+      mbar_init(&acc1_free[i], 1);
+      mbar_init(&drain[i], 1);
+    }
     for (int i = 0; i < 4; ++i) mbar_init(&h_full[i], kEpiWarps);
     mbar_init(a2_full, 1);
     mbar_init(a2_empty, kEpiWarps);
-    mbar_init(drain, 1);
-    mbar_init(bfree, kEpiWarps);
-    mbar_init(bready, kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -202,29 +213,12 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
   const int total = sched.total_tiles();
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------- W1 / X producer
     if (lane == 0) {
-      int64_t n1 = 0, n2 = 0, x_issued = 0;  // chunks loaded into each ring
+      RingPos w;
+      int loads = 0, x_issued = 0;
       int it = 0;
       bool ok = true;
-      // Loads one chunk into the next slot of a ring: per half, wait until
-      // the MMAs have read that half of the slot's previous chunk; the full
-      // barrier is armed once, for the whole chunk, before the first load.
-      auto load_chunk = [&](uint8_t* ring_base, size_t chunk_bytes, uint64_t* full,
-                            uint64_t* empty, int64_t& n, int where, auto&& issue_half) -> bool {
-        const int slot = (int)(n % P::NSLOT);
-        const uint32_t ph = (uint32_t)((n / P::NSLOT) & 1);
-        uint8_t* buf = ring_base + (size_t)slot * chunk_bytes;
-        for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&empty[2 * slot + h], ph ^ 1u, status, where, abort_flag)) return false;
-          if (h == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)chunk_bytes);
-          issue_half(buf, &full[slot], h);
-          // Counted once its first loads are in flight, so that the drain
-          // below waits for them even if the second half is never issued.
-          if (h == 0) ++n;
-        }
-        return true;
-      };
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         const TileCoord tc = sched.decode(t);
         const int gw = tc.g % Gw;
@@ -241,131 +235,162 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
             for (int kb = 0; kb < P::XK; ++kb) tma_prefetch_l2_2d(&tmX, kb * kBK, nx.row0);
           }
         }
-        for (int s = 0; s < nch + kLag && ok; ++s) {
-          if (s < nch) {  // W1 rows [s*128, +128): k-slabs [128 x 64], W1H per half
-            ok = load_chunk(ring1, P::W1C, full1, empty1, n1, 0x201,
-                            [&](uint8_t* buf, uint64_t* bar, int h) {
-                              for (int j = 0; j < P::W1H; ++j) {
-                                const int kb = h * P::W1H + j;
-                                tma_load_2d(buf + kb * kSlab, &tmW1, bar, kb * kBK,
-                                            gw * F + s * kFC);
-                              }
-                            });
-          }
-          if (s >= kLag && ok) {  // W2 [D rows, 64 k] k-slab h of chunk s-kLag
-            const int c = s - kLag;
-            ok = load_chunk(ring2, P::W2C, full2, empty2, n2, 0x203,
-                            [&](uint8_t* buf, uint64_t* bar, int h) {
-                              tma_load_2d(buf + h * P::W2H, &tmW2, bar, c * kFC + h * kBK,
-                                          gw * D);
-                            });
+        for (int c = 0; c < nch && ok; ++c) {
+          for (int h = 0; h < 2; ++h) {  // W1 rows [c*128, +128), K slabs of half h
+            if (!mbar_wait(&empty1[w.slot], w.phase ^ 1u, status, 0x201, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full1[w.slot], (uint32_t)P::W1H);
+            for (int j = 0; j < P::W1HS; ++j)
+              tma_load_2d(ring1 + w.slot * P::W1H + j * kSlab, &tmW1, &full1[w.slot],
+                          (h * P::W1HS + j) * kBK, gw * F + c * kFC);
+            ++loads;
+            w.next(kW1Slots);
           }
         }
       }
       // Let every load this thread issued land before the CTA can exit.
-      for (int i = 1; i <= P::NSLOT; ++i) {
-        if (n1 - i >= 0)
-          mbar_wait(&full1[(n1 - i) % P::NSLOT], (uint32_t)(((n1 - i) / P::NSLOT) & 1), status,
-                    0x204, nullptr);
-        if (n2 - i >= 0)
-          mbar_wait(&full2[(n2 - i) % P::NSLOT], (uint32_t)(((n2 - i) / P::NSLOT) & 1), status,
-                    0x204, nullptr);
+      RingPos d = w;
+      for (int i = 0; i < kW1Slots && i < loads; ++i) {
+        d.slot = (d.slot + kW1Slots - 1) % kW1Slots;
+        if (d.slot == kW1Slots - 1) d.phase ^= 1u;
+        mbar_wait(&full1[d.slot], d.phase, status, 0x204, nullptr);
       }
       if (x_issued > 0) mbar_wait(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x204, nullptr);
     }
+  } else if (warp == kProd2Warp) {
+    // ------------------------------------------------------------ W2 producer
+    if (lane == 0) {
+      RingPos w;
+      int loads = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int gw = sched.decode(t).g % Gw;
+        for (int c = 0; c < nch && ok; ++c) {
+          for (int h = 0; h < 2; ++h) {  // W2 [D rows, 64 k]: K columns [c*128 + 64h, +64)
+            if (!mbar_wait(&empty2[w.slot], w.phase ^ 1u, status, 0x203, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full2[w.slot], (uint32_t)P::W2H);
+            tma_load_2d(ring2 + w.slot * P::W2H, &tmW2, &full2[w.slot], c * kFC + h * kBK,
+                        gw * D);
+            ++loads;
+            w.next(kW2Slots);
+          }
+        }
+      }
+      RingPos d = w;
+      for (int i = 0; i < kW2Slots && i < loads; ++i) {
+        d.slot = (d.slot + kW2Slots - 1) % kW2Slots;
+        if (d.slot == kW2Slots - 1) d.phase ^= 1u;
+        mbar_wait(&full2[d.slot], d.phase, status, 0x204, nullptr);
+      }
+    }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ GEMM1 issuer
     if (lane == 0) {
       const uint32_t idesc1 = idesc_bf16_f32(kBM, 128);  // GEMM1: N = d_ff chunk
-      const uint32_t idesc2 = idesc_bf16_f32(kBM, D);    // GEMM2: N = d_model
-      int64_t n1 = 0, n2 = 0;  // chunks consumed from each weight ring
+      RingPos w;
       int it = 0;
       bool any = false, ok = true;
       const uint32_t x_addr = smem_u32(sx);
       const uint32_t ring1_addr = smem_u32(ring1);
-      const uint32_t ring2_addr = smem_u32(ring2);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         if (!mbar_wait(x_full, (uint32_t)(it & 1), status, 0x205, abort_flag)) break;
-        tc_fence_after();
-        for (int s = 0; s < nch + kLag && ok; ++s) {
-          if (s < nch) {  // GEMM1(s)
-            // acc1[b] last held H(s-2), read by GEMM2(s-2), which this
-            // thread issued before: no wait needed.
-            const int64_t gc = (int64_t)it * nch + s;
-            const int b = (int)(gc & 1);
-            const uint32_t d = tmem_base + kAcc1Col + (uint32_t)b * 128u;
-            const int slot = (int)(n1 % P::NSLOT);
-            if (!mbar_wait(&full1[slot], (uint32_t)((n1 / P::NSLOT) & 1), status, 0x207,
-                           abort_flag)) {
+        for (int c = 0; c < nch; ++c) {
+          const int gc = it * nch + c;
+          const int b = gc & 1;
+          // acc1[b] last held H(gc-2): GEMM2(gc-2), issued by the other
+          // thread, must have read it.
+          if (gc >= 2 && !mbar_wait(&acc1_free[b], (uint32_t)(((gc - 2) >> 1) & 1), status,
+                                    0x206, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t d = tmem_base + kAcc1Col + (uint32_t)b * 128u;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (!mbar_wait(&full1[w.slot], w.phase, status, 0x207, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t b0 = ring1_addr + (uint32_t)(slot * P::W1C);
+            const uint32_t b0 = ring1_addr + (uint32_t)(w.slot * P::W1H);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-#pragma unroll
-              for (int j = 0; j < P::W1H; ++j) {
-                const int kb = h * P::W1H + j;
-                const uint32_t a0 = x_addr + kb * kSlab;
-#pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk)
-                  umma_bf16(d, smem_desc_sw128(a0 + kk * 32),
-                            smem_desc_sw128(b0 + kb * kSlab + kk * 32), idesc1,
-                            (kb | kk) != 0 ? 1u : 0u);
-              }
-              umma_commit(&empty1[2 * slot + h]);
-            }
-            any = true;
-            ++n1;
-            umma_commit(&a1_full[b]);
-            if (s == nch - 1) umma_commit(x_empty);
-          }
-          if (s >= kLag) {  // GEMM2(s-kLag), N = D in one instruction, A = H in TMEM
-            const int c = s - kLag;
-            const int64_t gc = (int64_t)it * nch + c;
-            const int b = (int)(gc & 1);
-            const uint32_t k = (uint32_t)(gc >> 1);
-            if (c == 0) {
-              if (!mbar_wait(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x208, abort_flag)) {
-                ok = false;
-                break;
-              }
-            }
-            const int slot = (int)(n2 % P::NSLOT);
-            if (!mbar_wait(&full2[slot], (uint32_t)((n2 / P::NSLOT) & 1), status, 0x20a,
-                           abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint32_t h_tmem = tmem_base + kAcc1Col + (uint32_t)b * 128u;
-            const uint32_t b0 = ring2_addr + (uint32_t)(slot * P::W2C);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {  // K columns [64h, 64h+64) of the chunk = W2 k-slab h
-              if (!mbar_wait(&h_full[2 * b + h], k & 1u, status, 0x209, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
+            for (int j = 0; j < P::W1HS; ++j) {
+              const uint32_t a0 = x_addr + (h * P::W1HS + j) * kSlab;
 #pragma unroll
               for (int kk = 0; kk < kBK / 16; ++kk)
-                umma_bf16_ts(tmem_base, h_tmem + (uint32_t)(h * 64 + kk * 16),
-                             smem_desc_sw128(b0 + (uint32_t)(h * P::W2H) + kk * 32), idesc2,
-                             (c | h | kk) != 0 ? 1u : 0u);
-              umma_commit(&empty2[2 * slot + h]);
+                umma_bf16(d, smem_desc_sw128(a0 + kk * 32),
+                          smem_desc_sw128(b0 + j * kSlab + kk * 32), idesc1,
+                          (h | j | kk) != 0 ? 1u : 0u);
             }
-            if (!ok) break;
-            ++n2;
-            if (c == nch - 1) umma_commit(a2_full);
+            umma_commit(&empty1[w.slot]);
+            w.next(kW1Slots);
           }
+          if (!ok) break;
+          any = true;
+          umma_commit(&a1_full[b]);
+          if (c == nch - 1) umma_commit(x_empty);
         }
       }
       if (any) {
-        umma_commit(drain);
-        mbar_wait(drain, 0, status, 0x20b, nullptr);
+        umma_commit(&drain[0]);
+        mbar_wait(&drain[0], 0, status, 0x20b, nullptr);
       }
     }
-  } else if (GATHER && warp == kThreads / 32) {
+  } else if (warp == kIssue2Warp) {
+    // ------------------------------------------------------------ GEMM2 issuer
+    // GEMM2(c), N = D in one instruction, A = H(c) in TMEM.  Issued by its own
+    // thread, so that its waits (H from the epilogue, W2 from the producer)
+    // overlap the GEMM1s the other thread issues meanwhile.
+    if (lane == 0) {
+      const uint32_t idesc2 = idesc_bf16_f32(kBM, D);
+      RingPos w;
+      int it = 0;
+      bool any = false, ok = true;
+      const uint32_t ring2_addr = smem_u32(ring2);
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        for (int c = 0; c < nch && ok; ++c) {
+          const int gc = it * nch + c;
+          const int b = gc & 1;
+          const uint32_t k = (uint32_t)(gc >> 1);
+          if (c == 0 &&
+              !mbar_wait(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x208, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t h_tmem = tmem_base + kAcc1Col + (uint32_t)b * 128u;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // K columns [64h, 64h+64) of the chunk
+            if (!mbar_wait(&full2[w.slot], w.phase, status, 0x20a, abort_flag) ||
+                !mbar_wait(&h_full[2 * b + h], k & 1u, status, 0x209, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b0 = ring2_addr + (uint32_t)(w.slot * P::W2H);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_bf16_ts(tmem_base, h_tmem + (uint32_t)(h * 64 + kk * 16),
+                           smem_desc_sw128(b0 + kk * 32), idesc2, (c | h | kk) != 0 ? 1u : 0u);
+            umma_commit(&empty2[w.slot]);
+            w.next(kW2Slots);
+          }
+          if (!ok) break;
+          any = true;
+          umma_commit(&acc1_free[b]);  // H(gc) read: GEMM1(gc+2) may overwrite acc1[b]
+          if (c == nch - 1) umma_commit(a2_full);
+        }
+      }
+      if (any) {
+        umma_commit(&drain[1]);
+        mbar_wait(&drain[1], 0, status, 0x20b, nullptr);
+      }
+    }
+  } else if (GATHER && warp == kGatherWarp) {
     // ------------------------------------------------------------ row gather
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
@@ -412,39 +437,33 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
       fence_proxy_async_smem();
       warp_arrive(x_full, lane);
     }
-  } else {
+  } else if (warp >= 2 && warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
     // 16 warps: four per TMEM lane quadrant q; warp group `sub` owns chunk
     // columns [sub*32, sub*32+32) and output columns [sub*D/4, (sub+1)*D/4).
+    // Biases come straight from global memory (L1-resident per expert); a
+    // chunk's are fetched before its accumulator is waited for.
     const int ew = warp - 2;           // 0..15
     const int q = warp & 3;            // TMEM lane quadrant of this warp
     const int sub = ew >> 2;           // 0..3
     const int r = q * 32 + lane;       // tile row owned by this thread
-    const int etid = ew * 32 + lane;   // 0..511
     constexpr int kOutCols = D / 4;
     int it = 0;
-    int staged_gw = -1;
-    uint32_t n_staged = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
       const TileCoord tc = sched.decode(t);
       const int gw = tc.g % Gw;
-      if (gw != staged_gw) {  // the same decision in every epilogue thread
-        if (n_staged > 0) {   // everyone is done with the previous expert's biases
-          warp_arrive(bfree, lane);
-          if (!mbar_wait(bfree, (n_staged - 1) & 1u, status, 0x20f, abort_flag)) break;
-        }
-        for (int i = etid; i < F; i += kEpiThreads) b1s[i] = b1[(int64_t)gw * F + i];
-        for (int i = etid; i < D; i += kEpiThreads) b2s[i] = b2[(int64_t)gw * D + i];
-        warp_arrive(bready, lane);
-        if (!mbar_wait(bready, n_staged & 1u, status, 0x210, abort_flag)) break;
-        ++n_staged;
-        staged_gw = gw;
-      }
+      const float* b1e = b1 + (int64_t)gw * F;
       for (int c = 0; c < nch; ++c) {
-        const int64_t gc = (int64_t)it * nch + c;
-        const int b = (int)(gc & 1);
+        const int gc = it * nch + c;
+        const int b = gc & 1;
         const uint32_t k = (uint32_t)(gc >> 1);
+        float4 bias[2][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            bias[h][i] = __ldg(reinterpret_cast<const float4*>(b1e + c * kFC + h * 64 + sub * 16) + i);
         if (!mbar_wait(&a1_full[b], k & 1u, status, 0x20c, abort_flag)) {
           ok = false;
           break;
@@ -458,22 +477,25 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const float4* bc = reinterpret_cast<const float4*>(b1s + c * kFC + h * 64 + sub * 16);
           float a[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 bb = bc[i];
-            a[4 * i + 0] = __uint_as_float(v[h][4 * i + 0]) + bb.x;
-            a[4 * i + 1] = __uint_as_float(v[h][4 * i + 1]) + bb.y;
-            a[4 * i + 2] = __uint_as_float(v[h][4 * i + 2]) + bb.z;
-            a[4 * i + 3] = __uint_as_float(v[h][4 * i + 3]) + bb.w;
+          for (int i = 0; i < 4; ++i) {  // + b1, two values per packed add
+            const float4 bb = bias[h][i];
+            f2_unpack(f2_add(f2_pack(__uint_as_float(v[h][4 * i + 0]),
+                                     __uint_as_float(v[h][4 * i + 1])),
+                             f2_pack(bb.x, bb.y)),
+                      a[4 * i + 0], a[4 * i + 1]);
+            f2_unpack(f2_add(f2_pack(__uint_as_float(v[h][4 * i + 2]),
+                                     __uint_as_float(v[h][4 * i + 3])),
+                             f2_pack(bb.z, bb.w)),
+                      a[4 * i + 2], a[4 * i + 3]);
           }
           act_n<16>(act, a);
-          uint32_t w[8];
+          uint32_t wv[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
+          for (int i = 0; i < 8; ++i) wv[i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
           // Half h of H(c): into the first 8 of this thread's 16 columns.
-          tmem_st_32x32b_x8(tbase + (uint32_t)(h * 64), w);
+          tmem_st_32x32b_x8(tbase + (uint32_t)(h * 64), wv);
           tmem_st_wait();
           tc_fence_before();
           warp_arrive(&h_full[2 * b + h], lane);
@@ -482,6 +504,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
       if (!ok) break;
 
       // Output: acc2 + b2 -> bf16 rows of Y.
+      const float4* bo4 = reinterpret_cast<const float4*>(b2 + (int64_t)gw * D + sub * kOutCols);
       if (!mbar_wait(a2_full, (uint32_t)(it & 1), status, 0x20e, abort_flag)) break;
       tc_fence_after();
       uint32_t o[kOutCols];
@@ -497,19 +520,15 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
       tc_fence_before();
       warp_arrive(a2_empty, lane);
       if (r < tc.rows) {
-        const float* bo = b2s + sub * kOutCols;
         uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)tc.row0 + r) * D + sub * kOutCols);
 #pragma unroll
         for (int j = 0; j < kOutCols / 8; ++j) {
+          const float4 c0 = __ldg(bo4 + 2 * j), c1 = __ldg(bo4 + 2 * j + 1);
           uint4 pk;
-          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + bo[8 * j],
-                             __uint_as_float(o[8 * j + 1]) + bo[8 * j + 1]);
-          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + bo[8 * j + 2],
-                             __uint_as_float(o[8 * j + 3]) + bo[8 * j + 3]);
-          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + bo[8 * j + 4],
-                             __uint_as_float(o[8 * j + 5]) + bo[8 * j + 5]);
-          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + bo[8 * j + 6],
-                             __uint_as_float(o[8 * j + 7]) + bo[8 * j + 7]);
+          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + c0.x, __uint_as_float(o[8 * j + 1]) + c0.y);
+          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + c0.z, __uint_as_float(o[8 * j + 3]) + c0.w);
+          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + c1.x, __uint_as_float(o[8 * j + 5]) + c1.y);
+          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + c1.z, __uint_as_float(o[8 * j + 7]) + c1.w);
           dst[j] = pk;
         }
       }

@@ -2,36 +2,41 @@
 //
 //   Y[rows] = act(Xp[rows] @ W1[e]^T + b1[e]) @ W2[e]^T + b2[e],
 //
-// with one tcgen05.mma.cta_group::2 instruction stream for both SMs of a
-// thread-block cluster of two.  The same schedule as fused_ffn.cu (d_ff in
-// 128-wide chunks c; GEMM1(c) -> acc1 in TMEM; bias + GELU -> bf16 H(c)
-// written back into TMEM; GEMM2(c) reads A = H(c) from TMEM and accumulates
-// acc2 = Y in TMEM; GEMM2(c) issued after GEMM1(c+1)), but on pairs:
+// issued as one tcgen05.mma.cta_group::2 stream for both SMs of a
+// thread-block cluster of two.  Every MMA is M = 256 (128 rows per SM) x
+// N = 256 x K = 16, so each instruction gives each SM 128 cycles of tensor
+// work - more than the ~100-cycle issue interval of a pair MMA, and enough to
+// hide the barrier tests of the issuing thread.
 //
-//   * each CTA holds its own 128 rows of the tile (X in shared memory; acc1,
-//     H and acc2 in its TMEM), and HALF of every weight chunk: rows
-//     [64r, 64r + 64) of the W1 chunk and rows [128r, 128r + 128) of the W2
-//     chunk, r = its rank in the pair.  One M = 256 MMA reads A from both
-//     CTAs and B from both halves, so each SM streams half as many weight
-//     bytes per FLOP as the one-CTA kernel, and the shared-memory operand
-//     reads of GEMM1 drop from 128 to 96 bytes per clock at full tensor rate;
-//   * the freed shared memory double-buffers both weight rings (two
-//     whole-chunk slots each), so the next chunk's weights load while the
-//     current one is multiplied;
-//   * the even CTA (leader) issues every MMA.  Barriers it waits on live in
-//     its shared memory: the peer's TMA loads complete on them
-//     (cp.async.bulk.tensor ... .cta_group::2) and the peer's epilogue warps
-//     arrive on them through shared::cluster addresses.  MMA completions
-//     that both CTAs wait for are committed twice, once to each CTA's copy
-//     of the barrier.
+// Per tile, d_ff is processed in 256-wide chunks c:
+//   GEMM1(c): acc1 (TMEM, 256 fp32 columns) = X[256, D] @ W1[e][c*256:+256, :]^T
+//   epilogue: acc1 -> registers (acc1 is free again at once) -> +b1 -> GELU
+//             -> bf16 H(c) in shared memory, one 64-wide K slab at a time
+//   GEMM2(c): acc2 (TMEM, D = 256 columns) += H(c) @ W2[e][:, c*256:+256]^T,
+//             slab by slab as the epilogue finishes each
+// The MMA thread issues GEMM1(c+1) as soon as the epilogue has drained
+// acc1, then GEMM2(c): the tensor core runs GEMM1(c+1) while the epilogue
+// turns chunk c into H(c).  After the last chunk, acc2 + b2 goes to Y.
 //
-// Roles per CTA (576 threads): warp 0 TMA producer (its X rows and its
-// weight halves), warp 1 TMEM allocation for the pair and, in the leader,
-// the MMA issuer, warps 2-17 epilogue (its 128 rows of acc1/H and acc2).
-// TMEM per CTA: acc2 in columns [0, 256), acc1 buffers at 256 and 384.
-// Shared memory per CTA: X 64 KB + W1 ring 2 x 32 KB + W2 ring 2 x 32 KB +
-// biases 5 KB + scheduler 2 KB.  d_model 256, d_ff a multiple of 128 up to
-// 1024.
+// The pair: each CTA holds its own 128 rows (X and H in its shared memory,
+// acc1 / acc2 in its TMEM) and HALF of every weight K-slab ([128 x 64]: the
+// W1 rows [c*256 + 128r, +128) or the W2 output rows [128r, +128) of the
+// chunk, r = its rank), so each SM streams half the weight bytes per FLOP of
+// a one-SM tile.  Weights stream through a ring of kRing K-slabs in the
+// order the MMAs consume them (GEMM1(c) slabs, then GEMM2(c-1) slabs).  The
+// even CTA (leader) issues every MMA; the barriers it waits on live in its
+// shared memory - the peer's TMA loads complete on them (.cta_group::2) and
+// the peer's epilogue warps arrive on them through shared::cluster
+// addresses; MMA completions that both CTAs wait for are committed twice,
+// once to each CTA's copy of the barrier.
+//
+// Roles per CTA (576 threads): warp 0 TMA producer, warp 1 TMEM allocation
+// for the pair and (leader) MMA issuer, warps 2-17 epilogue.  Epilogue warp
+// (lane quadrant q, group s) owns rows 32q..32q+31 and, of every 64-wide
+// K slab, columns [16s, 16s + 16).
+// TMEM per CTA: acc2 columns [0, 256), acc1 [256, 512).
+// Shared memory per CTA: X 64 KB + ring 5 x 16 KB + H 64 KB + biases 5 KB +
+// scheduler 2 KB.  d_model 256; d_ff a multiple of 256 up to 1024.
 //
 // Every wait is bounded (common.cuh); a CTA that gives up sets its abort
 // flag, its roles unwind, the peer's waits run out in turn, and both CTAs
@@ -46,24 +51,22 @@ namespace {
 
 constexpr int kPD = 256;               // d_model
 constexpr int kPBM = 128;              // rows per CTA; a pair tile has 256
-constexpr int kPFC = 128;              // d_ff chunk
+constexpr int kPFC = 256;              // d_ff chunk
 constexpr int kPBK = 64;               // bf16 per 128-byte swizzled row
-constexpr int kPXK = kPD / kPBK;       // 4 X k-slabs
+constexpr int kPSlabs = kPD / kPBK;    // 4 K slabs of X, of a W1 chunk, of a W2 chunk, of H
 constexpr int kPEpiWarps = 16;
 constexpr int kPThreads = 64 + kPEpiWarps * 32;
 constexpr int kPMaxF = 1024;
-constexpr int kPNSlot = 2;
+constexpr int kRing = 5;               // weight K slabs in flight
 constexpr uint32_t kPAcc1Col = 256;
 using PSched = GroupSchedT<256>;
 
-constexpr size_t kPXSlab = (size_t)kPBM * kPBK * 2;          // 16 KB: [128 x 64]
-constexpr size_t kPXBytes = kPXK * kPXSlab;                   // 64 KB
-constexpr size_t kPW1Slab = (size_t)(kPFC / 2) * kPBK * 2;    // 8 KB: [64 x 64]
-constexpr size_t kPW1Slot = kPXK * kPW1Slab;                  // 32 KB: half a W1 chunk
-constexpr size_t kPW2Slab = (size_t)(kPD / 2) * kPBK * 2;     // 16 KB: [128 x 64]
-constexpr size_t kPW2Slot = 2 * kPW2Slab;                     // 32 KB: half a W2 chunk
+constexpr size_t kPSlab = (size_t)kPBM * kPBK * 2;            // 16 KB: [128 x 64] bf16
+constexpr size_t kPXBytes = kPSlabs * kPSlab;                  // 64 KB
+constexpr size_t kPHBytes = kPSlabs * kPSlab;                  // 64 KB
+constexpr size_t kPRingBytes = kRing * kPSlab;                 // 80 KB
 constexpr size_t kPBias = (size_t)(kPMaxF + kPD) * 4;
-constexpr size_t kPSmem = 1024 + kPXBytes + kPNSlot * (kPW1Slot + kPW2Slot) + kPBias +
+constexpr size_t kPSmem = 1024 + kPXBytes + kPHBytes + kPRingBytes + kPBias +
                           PSched::smem_bytes() + 512;
 static_assert(kPSmem <= 232448, "shared memory per CTA");
 
@@ -84,6 +87,11 @@ CTI_DEVICE void commit_both(uint64_t* bar) {
   umma_commit_pair(mapa_shared(bar, 1));
 }
 
+// 16-byte store into a 128-byte-swizzled K-major slab: row r, chunk j.
+CTI_DEVICE void st_swizzled16(uint8_t* slab, int r, int j, uint4 v) {
+  *reinterpret_cast<uint4*>(slab + r * 128 + ((j ^ (r & 7)) << 4)) = v;
+}
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     fused_ffn_pair_kernel(const __grid_constant__ CUtensorMap tmX,
                           const __grid_constant__ CUtensorMap tmW1,
@@ -96,25 +104,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sx = smem;
-  uint8_t* ring1 = sx + kPXBytes;                       // W1 halves
-  uint8_t* ring2 = ring1 + kPNSlot * kPW1Slot;          // W2 halves
-  float* b1s = reinterpret_cast<float*>(ring2 + kPNSlot * kPW2Slot);
+  uint8_t* sh = sx + kPXBytes;          // H(c): 4 K slabs [128 x 64]
+  uint8_t* ring = sh + kPHBytes;        // weight K slabs
+  float* b1s = reinterpret_cast<float*>(ring + kPRingBytes);
   float* b2s = b1s + kPMaxF;
   uint8_t* sched_mem = reinterpret_cast<uint8_t*>(b2s + kPD);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + PSched::smem_bytes());
   // Waited on by the leader's MMA thread (arrivals and bytes from both CTAs):
-  uint64_t* full1 = bars;            // [2] W1 halves of both CTAs landed
-  uint64_t* full2 = full1 + 2;       // [2] W2 halves landed
-  uint64_t* x_full = full2 + 2;      // X rows of both CTAs landed
-  uint64_t* h_full = x_full + 1;     // [2][2] half h of H(c) written by both epilogues
-  uint64_t* a2_empty = h_full + 4;   // both epilogues have read acc2
+  uint64_t* full = bars;                 // [kRing] weight slab of both CTAs landed
+  uint64_t* x_full = full + kRing;       // X rows of both CTAs landed
+  uint64_t* acc1_free = x_full + 1;      // both epilogues have drained acc1
+  uint64_t* h_full = acc1_free + 1;      // [4] H slab written by both epilogues
+  uint64_t* a2_empty = h_full + kPSlabs; // both epilogues have read acc2
   uint64_t* drain = a2_empty + 1;
   // Waited on in each CTA (committed by the leader to both copies):
-  uint64_t* empty1 = drain + 1;      // [2] a W1 slot may be refilled
-  uint64_t* empty2 = empty1 + 2;     // [2]
-  uint64_t* x_empty = empty2 + 2;
-  uint64_t* a1_full = x_empty + 1;   // [2] GEMM1(c) done
-  uint64_t* a2_full = a1_full + 2;   // GEMM2 of the tile's last chunk done
+  uint64_t* empty = drain + 1;           // [kRing] weight slot may be refilled
+  uint64_t* x_empty = empty + kRing;
+  uint64_t* a1_full = x_empty + 1;       // GEMM1(c) done
+  uint64_t* h_empty = a1_full + 1;       // [4] GEMM2 has read H slab kb
+  uint64_t* a2_full = h_empty + kPSlabs; // GEMM2 of the tile's last chunk done
   // Local to the epilogue of each CTA:
   uint64_t* bfree = a2_full + 1;
   uint64_t* bready = bfree + 1;
@@ -130,18 +138,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPNSlot; ++s) {
-      mbar_init(&full1[s], 1);
-      mbar_init(&full2[s], 1);
-      mbar_init(&empty1[s], 1);
-      mbar_init(&empty2[s], 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&h_full[i], 2 * kPEpiWarps);
+    mbar_init(acc1_free, 2 * kPEpiWarps);
+    for (int i = 0; i < kPSlabs; ++i) {
+      mbar_init(&h_full[i], 2 * kPEpiWarps);
+      mbar_init(&h_empty[i], 1);
+    }
     mbar_init(a2_empty, 2 * kPEpiWarps);
     mbar_init(drain, 1);
-    for (int i = 0; i < 2; ++i) mbar_init(&a1_full[i], 1);
+    mbar_init(a1_full, 1);
     mbar_init(a2_full, 1);
     mbar_init(bfree, kPEpiWarps);
     mbar_init(bready, kPEpiWarps);
@@ -172,173 +182,160 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint32_t full1_c[2] = {mapa_shared(&full1[0], 0), mapa_shared(&full1[1], 0)};
-      const uint32_t full2_c[2] = {mapa_shared(&full2[0], 0), mapa_shared(&full2[1], 0)};
+      uint32_t full_c[kRing];
+      for (int s = 0; s < kRing; ++s) full_c[s] = mapa_shared(&full[s], 0);
       const uint32_t x_full_c = mapa_shared(x_full, 0);
-      int n1 = 0, n2 = 0, x_issued = 0;
+      int n = 0, x_issued = 0;  // weight slabs issued, X tiles issued
       int it = 0;
       bool ok = true;
+      // One weight K slab (this CTA's [128 x 64] half) into the next ring slot.
+      auto load_slab = [&](const CUtensorMap* map, int k0, int row0) -> bool {
+        const int slot = n % kRing;
+        if (!mbar_wait_cluster(&empty[slot], (uint32_t)((n / kRing) & 1) ^ 1u, status, 0x401,
+                               abort_flag))
+          return false;
+        if (leader) mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * kPSlab));
+        tma_load_2d_pair(ring + slot * kPSlab, map, full_c[slot], k0, row0);
+        ++n;
+        return true;
+      };
       for (int t = pair; t < total && ok; t += npairs, ++it) {
         const TileCoord tc = sched.decode(t);
         const int gw = tc.g % Gw;
         const int my_row0 = tc.row0 + (int)rank * kPBM;
-        if (!mbar_wait_cluster(x_empty, (uint32_t)(it & 1) ^ 1u, status, 0x302, abort_flag)) break;
+        if (!mbar_wait_cluster(x_empty, (uint32_t)(it & 1) ^ 1u, status, 0x402, abort_flag)) break;
         if (leader) mbar_arrive_expect_tx(x_full, (uint32_t)(2 * kPXBytes));
-        for (int kb = 0; kb < kPXK; ++kb)
-          tma_load_2d_pair(sx + kb * kPXSlab, &tmX, x_full_c, kb * kPBK, my_row0);
+        for (int kb = 0; kb < kPSlabs; ++kb)
+          tma_load_2d_pair(sx + kb * kPSlab, &tmX, x_full_c, kb * kPBK, my_row0);
         ++x_issued;
         if (t + npairs < total) {  // the next tile's rows into L2
           const TileCoord nx = sched.decode(t + npairs);
-          for (int kb = 0; kb < kPXK; ++kb)
+          for (int kb = 0; kb < kPSlabs; ++kb)
             tma_prefetch_l2_2d(&tmX, kb * kPBK, nx.row0 + (int)rank * kPBM);
         }
-        for (int s = 0; s <= nch && ok; ++s) {
-          if (s < nch) {  // this CTA's half of W1 chunk s
-            const int slot = n1 & 1;
-            if (!mbar_wait_cluster(&empty1[slot], (uint32_t)((n1 >> 1) & 1) ^ 1u, status, 0x301,
-                                   abort_flag)) {
-              ok = false;
-              break;
-            }
-            if (leader) mbar_arrive_expect_tx(&full1[slot], (uint32_t)(2 * kPW1Slot));
-            uint8_t* buf = ring1 + slot * kPW1Slot;
-            for (int kb = 0; kb < kPXK; ++kb)
-              tma_load_2d_pair(buf + kb * kPW1Slab, &tmW1, full1_c[slot], kb * kPBK,
-                               gw * F + s * kPFC + (int)rank * (kPFC / 2));
-            ++n1;
-          }
-          if (s >= 1) {  // this CTA's half of W2 chunk s-1: output rows [128r, +128)
-            const int c = s - 1;
-            const int slot = n2 & 1;
-            if (!mbar_wait_cluster(&empty2[slot], (uint32_t)((n2 >> 1) & 1) ^ 1u, status, 0x303,
-                                   abort_flag)) {
-              ok = false;
-              break;
-            }
-            if (leader) mbar_arrive_expect_tx(&full2[slot], (uint32_t)(2 * kPW2Slot));
-            uint8_t* buf = ring2 + slot * kPW2Slot;
-            for (int h = 0; h < 2; ++h)
-              tma_load_2d_pair(buf + h * kPW2Slab, &tmW2, full2_c[slot], c * kPFC + h * kPBK,
-                               gw * kPD + (int)rank * (kPD / 2));
-            ++n2;
-          }
+        // The MMAs' order: GEMM1(c) slabs, then GEMM2(c-1) slabs.
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch)
+            for (int kb = 0; kb < kPSlabs && ok; ++kb)
+              ok = load_slab(&tmW1, kb * kPBK, gw * F + c * kPFC + (int)rank * kPBM);
+          if (c >= 1)
+            for (int kb = 0; kb < kPSlabs && ok; ++kb)
+              ok = load_slab(&tmW2, (c - 1) * kPFC + kb * kPBK, gw * kPD + (int)rank * kPBM);
         }
       }
       // The leader's full barriers count both CTAs' bytes: once their last
       // armed phases complete, no load of either CTA is in flight.
       if (leader) {
-        for (int i = 1; i <= kPNSlot; ++i) {
-          if (n1 - i >= 0)
-            mbar_wait_cluster(&full1[(n1 - i) & 1], (uint32_t)(((n1 - i) >> 1) & 1), status,
-                              0x304, nullptr);
-          if (n2 - i >= 0)
-            mbar_wait_cluster(&full2[(n2 - i) & 1], (uint32_t)(((n2 - i) >> 1) & 1), status,
-                              0x304, nullptr);
-        }
+        for (int i = 1; i <= kRing; ++i)
+          if (n - i >= 0)
+            mbar_wait_cluster(&full[(n - i) % kRing], (uint32_t)(((n - i) / kRing) & 1), status,
+                              0x403, nullptr);
         if (x_issued > 0)
-          mbar_wait_cluster(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x304, nullptr);
+          mbar_wait_cluster(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x403, nullptr);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
-      const uint32_t idesc1 = idesc_bf16_f32(2 * kPBM, kPFC);  // GEMM1: M 256, N 128
-      const uint32_t idesc2 = idesc_bf16_f32(2 * kPBM, kPD);   // GEMM2: M 256, N 256
-      int n1 = 0, n2 = 0;
+      const uint32_t idesc = idesc_bf16_f32(2 * kPBM, 256);  // M 256, N 256 (both GEMMs)
+      int n = 0;        // weight slabs consumed
+      int gc = 0;       // GEMM1s issued (global chunk counter)
       int it = 0;
       bool any = false, ok = true;
       const uint32_t x_addr = smem_u32(sx);
-      const uint32_t ring1_addr = smem_u32(ring1);
-      const uint32_t ring2_addr = smem_u32(ring2);
+      const uint32_t h_addr = smem_u32(sh);
+      const uint32_t ring_addr = smem_u32(ring);
+      const uint32_t acc1 = tmem_base + kPAcc1Col;
+      auto wait_slab = [&](uint32_t& b_addr) -> bool {
+        const int slot = n % kRing;
+        if (!mbar_wait_cluster(&full[slot], (uint32_t)((n / kRing) & 1), status, 0x405,
+                               abort_flag))
+          return false;
+        b_addr = ring_addr + (uint32_t)(slot * kPSlab);
+        return true;
+      };
+      auto release_slab = [&]() {
+        commit_both(&empty[n % kRing]);
+        ++n;
+      };
       for (int t = pair; t < total && ok; t += npairs, ++it) {
-        if (!mbar_wait_cluster(x_full, (uint32_t)(it & 1), status, 0x305, abort_flag)) break;
+        if (!mbar_wait_cluster(x_full, (uint32_t)(it & 1), status, 0x404, abort_flag)) break;
         tc_fence_after();
-        for (int s = 0; s <= nch && ok; ++s) {
-          if (s < nch) {  // GEMM1(s) into acc1[(it*nch + s) % 2]
-            const int b = (it * nch + s) & 1;
-            const uint32_t d = tmem_base + kPAcc1Col + (uint32_t)b * 128u;
-            const int slot = n1 & 1;
-            if (!mbar_wait_cluster(&full1[slot], (uint32_t)((n1 >> 1) & 1), status, 0x307,
-                                   abort_flag)) {
+        for (int c = 0; c <= nch && ok; ++c) {
+          if (c < nch) {  // GEMM1(c) into acc1, once both epilogues have drained it
+            if (gc > 0 && !mbar_wait_cluster(acc1_free, (uint32_t)((gc - 1) & 1), status, 0x406,
+                                             abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t b0 = ring1_addr + (uint32_t)(slot * kPW1Slot);
-#pragma unroll
-            for (int kb = 0; kb < kPXK; ++kb) {
-#pragma unroll
-              for (int kk = 0; kk < kPBK / 16; ++kk)
-                umma_bf16_pair(d, smem_desc_sw128(x_addr + kb * kPXSlab + kk * 32),
-                               smem_desc_sw128(b0 + kb * kPW1Slab + kk * 32), idesc1,
-                               (kb | kk) != 0 ? 1u : 0u);
-            }
-            commit_both(&empty1[slot]);
-            commit_both(&a1_full[b]);
-            if (s == nch - 1) commit_both(x_empty);
-            any = true;
-            ++n1;
-          }
-          if (s >= 1) {  // GEMM2(s-1): acc2 += H(s-1) @ W2 chunk, A from TMEM
-            const int c = s - 1;
-            const int gc = it * nch + c;
-            const int b = gc & 1;
-            const uint32_t k = (uint32_t)(gc >> 1);
-            if (c == 0 &&
-                !mbar_wait_cluster(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x308, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const int slot = n2 & 1;
-            if (!mbar_wait_cluster(&full2[slot], (uint32_t)((n2 >> 1) & 1), status, 0x30a,
-                                   abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint32_t h_tmem = tmem_base + kPAcc1Col + (uint32_t)b * 128u;
-            const uint32_t b0 = ring2_addr + (uint32_t)(slot * kPW2Slot);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (!mbar_wait_cluster(&h_full[2 * b + h], k & 1u, status, 0x309, abort_flag)) {
+            for (int kb = 0; kb < kPSlabs && ok; ++kb) {
+              uint32_t b0;
+              if (!wait_slab(b0)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < kPBK / 16; ++kk)
-                umma_bf16_ts_pair(tmem_base, h_tmem + (uint32_t)(h * 64 + kk * 16),
-                                  smem_desc_sw128(b0 + (uint32_t)(h * kPW2Slab) + kk * 32),
-                                  idesc2, (c | h | kk) != 0 ? 1u : 0u);
+                umma_bf16_pair(acc1, smem_desc_sw128(x_addr + kb * kPSlab + kk * 32),
+                               smem_desc_sw128(b0 + kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
+              release_slab();
             }
             if (!ok) break;
-            commit_both(&empty2[slot]);
-            if (c == nch - 1) commit_both(a2_full);
-            ++n2;
+            commit_both(a1_full);
+            if (c == nch - 1) commit_both(x_empty);
+            ++gc;
+            any = true;
+          }
+          if (c >= 1) {  // GEMM2(c-1): acc2 += H(c-1) @ W2 chunk, slab by slab
+            const int cc = c - 1;
+            const uint32_t hph = (uint32_t)((it * nch + cc) & 1);  // H of global chunk it*nch+cc
+            if (cc == 0 &&
+                !mbar_wait_cluster(a2_empty, (uint32_t)(it & 1) ^ 1u, status, 0x407, abort_flag)) {
+              ok = false;
+              break;
+            }
+            for (int kb = 0; kb < kPSlabs && ok; ++kb) {
+              uint32_t b0;
+              if (!wait_slab(b0) ||
+                  !mbar_wait_cluster(&h_full[kb], hph, status, 0x408, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < kPBK / 16; ++kk)
+                umma_bf16_pair(tmem_base, smem_desc_sw128(h_addr + kb * kPSlab + kk * 32),
+                               smem_desc_sw128(b0 + kk * 32), idesc,
+                               (cc | kb | kk) != 0 ? 1u : 0u);
+              release_slab();
+              commit_both(&h_empty[kb]);
+            }
+            if (!ok) break;
+            if (cc == nch - 1) commit_both(a2_full);
           }
         }
       }
       if (any) {
         umma_commit_pair(mapa_shared(drain, 0));
-        mbar_wait_cluster(drain, 0, status, 0x30b, nullptr);
+        mbar_wait_cluster(drain, 0, status, 0x409, nullptr);
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // 16 warps: four per TMEM lane quadrant q; warp group `sub` owns chunk
-    // columns [sub*16, +16) of each 64-column half and output columns
-    // [sub*64, +64).  H(c) half h goes into the first 8 of the thread's 16
-    // columns of that half, so GEMM2's K step kk of half h reads 8
-    // contiguous columns at 64h + 16kk (the layout of fused_ffn.cu).
     const int ew = warp - 2;
-    const int q = warp & 3;
-    const int sub = ew >> 2;
-    const int r = q * 32 + lane;
+    const int q = warp & 3;            // TMEM lane quadrant
+    const int sub = ew >> 2;           // columns [16 sub, +16) of every K slab
+    const int r = q * 32 + lane;       // row of this CTA's 128
     const int etid = ew * 32 + lane;
     constexpr int kOutCols = kPD / 4;
-    const uint32_t h_full_c[4] = {mapa_shared(&h_full[0], 0), mapa_shared(&h_full[1], 0),
-                                  mapa_shared(&h_full[2], 0), mapa_shared(&h_full[3], 0)};
+    uint32_t h_full_c[kPSlabs];
+    for (int i = 0; i < kPSlabs; ++i) h_full_c[i] = mapa_shared(&h_full[i], 0);
+    const uint32_t acc1_free_c = mapa_shared(acc1_free, 0);
     const uint32_t a2_empty_c = mapa_shared(a2_empty, 0);
-    int it = 0;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    int it = 0, gc = 0;
     int staged_gw = -1;
     uint32_t n_staged = 0;
     bool ok = true;
@@ -350,59 +347,74 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       if (gw != staged_gw) {
         if (n_staged > 0) {
           pair_warp_arrive_local(bfree, lane);
-          if (!mbar_wait(bfree, (n_staged - 1) & 1u, status, 0x30f, abort_flag)) break;
+          if (!mbar_wait(bfree, (n_staged - 1) & 1u, status, 0x40f, abort_flag)) break;
         }
         for (int i = etid; i < F; i += kPEpiWarps * 32) b1s[i] = b1[(int64_t)gw * F + i];
         for (int i = etid; i < kPD; i += kPEpiWarps * 32) b2s[i] = b2[(int64_t)gw * kPD + i];
         pair_warp_arrive_local(bready, lane);
-        if (!mbar_wait(bready, n_staged & 1u, status, 0x310, abort_flag)) break;
+        if (!mbar_wait(bready, n_staged & 1u, status, 0x410, abort_flag)) break;
         ++n_staged;
         staged_gw = gw;
       }
-      for (int c = 0; c < nch; ++c) {
-        const int gc = it * nch + c;
-        const int b = gc & 1;
-        const uint32_t k = (uint32_t)(gc >> 1);
-        if (!mbar_wait_cluster(&a1_full[b], k & 1u, status, 0x30c, abort_flag)) {
+      for (int c = 0; c < nch; ++c, ++gc) {
+        if (!mbar_wait_cluster(a1_full, (uint32_t)(gc & 1), status, 0x40c, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + kPAcc1Col +
-                               (uint32_t)b * 128u + (uint32_t)sub * 16u;
-        uint32_t v[2][16];
-        tmem_ld_32x32b_x16(tbase, v[0]);
-        tmem_ld_32x32b_x16(tbase + 64u, v[1]);
-        tmem_ld_wait();
+        // Drain this thread's 64 columns of acc1, then hand acc1 back.
+        uint32_t v[kPSlabs][16];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float4* bc = reinterpret_cast<const float4*>(b1s + c * kPFC + h * 64 + sub * 16);
+        for (int kb = 0; kb < kPSlabs; ++kb)
+          tmem_ld_32x32b_x16(lane_base + kPAcc1Col + (uint32_t)(kb * kPBK + sub * 16), v[kb]);
+        tmem_ld_wait();
+        tc_fence_before();
+        pair_warp_arrive_remote(acc1_free_c, lane);
+#pragma unroll
+        for (int kb = 0; kb < kPSlabs; ++kb) {
+          const float4* bc =
+              reinterpret_cast<const float4*>(b1s + c * kPFC + kb * kPBK + sub * 16);
           float a[16];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float4 bb = bc[i];
-            a[4 * i + 0] = __uint_as_float(v[h][4 * i + 0]) + bb.x;
-            a[4 * i + 1] = __uint_as_float(v[h][4 * i + 1]) + bb.y;
-            a[4 * i + 2] = __uint_as_float(v[h][4 * i + 2]) + bb.z;
-            a[4 * i + 3] = __uint_as_float(v[h][4 * i + 3]) + bb.w;
+            a[4 * i + 0] = __uint_as_float(v[kb][4 * i + 0]) + bb.x;
+            a[4 * i + 1] = __uint_as_float(v[kb][4 * i + 1]) + bb.y;
+            a[4 * i + 2] = __uint_as_float(v[kb][4 * i + 2]) + bb.z;
+            a[4 * i + 3] = __uint_as_float(v[kb][4 * i + 3]) + bb.w;
           }
           act_n<16>(act, a);
-          uint32_t w[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(a[2 * i], a[2 * i + 1]);
-          tmem_st_32x32b_x8(tbase + (uint32_t)(h * 64), w);
-          tmem_st_wait();
-          tc_fence_before();
-          pair_warp_arrive_remote(h_full_c[2 * b + h], lane);
+          uint4 w0, w1;
+          w0.x = pack_bf16x2(a[0], a[1]);
+          w0.y = pack_bf16x2(a[2], a[3]);
+          w0.z = pack_bf16x2(a[4], a[5]);
+          w0.w = pack_bf16x2(a[6], a[7]);
+          w1.x = pack_bf16x2(a[8], a[9]);
+          w1.y = pack_bf16x2(a[10], a[11]);
+          w1.z = pack_bf16x2(a[12], a[13]);
+          w1.w = pack_bf16x2(a[14], a[15]);
+          // GEMM2 of the previous chunk must be done with slab kb of H.
+          if (gc > 0 &&
+              !mbar_wait_cluster(&h_empty[kb], (uint32_t)((gc - 1) & 1), status, 0x40d,
+                                 abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* slab = sh + kb * kPSlab;
+          st_swizzled16(slab, r, 2 * sub, w0);
+          st_swizzled16(slab, r, 2 * sub + 1, w1);
+          fence_proxy_async_smem();  // visible to the tensor core's operand reads
+          pair_warp_arrive_remote(h_full_c[kb], lane);
         }
+        if (!ok) break;
       }
       if (!ok) break;
 
       // Output: acc2 + b2 -> bf16 rows of Y (this CTA's rows of the tile).
-      if (!mbar_wait_cluster(a2_full, (uint32_t)(it & 1), status, 0x30e, abort_flag)) break;
+      if (!mbar_wait_cluster(a2_full, (uint32_t)(it & 1), status, 0x40e, abort_flag)) break;
       tc_fence_after();
       uint32_t o[kOutCols];
-      const uint32_t taddr2 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)sub * kOutCols;
+      const uint32_t taddr2 = lane_base + (uint32_t)sub * kOutCols;
 #pragma unroll
       for (int j = 0; j < kOutCols / 32; ++j) {
         uint32_t tmp[32];
@@ -434,7 +446,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   }
 
   // Neither CTA leaves (or frees the pair's TMEM) while the other may still
-  // signal its barriers or read its tensor memory.
+  // signal its barriers or read its shared or tensor memory.
   tc_fence_before();
   __syncthreads();
   cluster_sync();
@@ -447,14 +459,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
 }  // namespace
 
-// The pair kernel for d_model 256 (the host checks the shape).
+// The pair kernel (the host checks the shape: d_model 256, d_ff % 256 == 0).
 int launch_fused_pair(const void* Xp, const void* W1, const float* b1, const void* W2,
                       const float* b2, const int32_t* offs, int G, int Gw, int64_t rows_total,
                       int F, int act, void* Y, int32_t* status, cudaStream_t s) {
   CUtensorMap tmX, tmW1, tmW2;
   if (!make_tmap_bf16_2d(&tmX, Xp, (uint64_t)rows_total, kPD, kPD, kPBM, kPBK) ||
-      !make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, kPD, kPD, kPFC / 2, kPBK) ||
-      !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * kPD, (uint64_t)F, (uint64_t)F, kPD / 2, kPBK))
+      !make_tmap_bf16_2d(&tmW1, W1, (uint64_t)Gw * F, kPD, kPD, kPBM, kPBK) ||
+      !make_tmap_bf16_2d(&tmW2, W2, (uint64_t)Gw * kPD, (uint64_t)F, (uint64_t)F, kPBM, kPBK))
     return CTI_ERR_INVALID_ARG;
   static uint64_t configured = 0;
   if (ensure_smem_limit(fused_ffn_pair_kernel, (int)kPSmem, configured) != cudaSuccess)

@@ -202,7 +202,19 @@ class CTRModel(nn.Module):
             m.gate = g.float()
             m.prepare_for_inference()
         self.seq_encoder.prepare_for_inference()
+        self._prepare_head()
         return self
+
+    @torch.no_grad()
+    def _prepare_head(self) -> None:
+        """The head's weights as the fused head kernel takes them: W1 bf16,
+        b1 / w2 / b2 fp32."""
+        l1, l2 = self.linear[0], self.linear[2]
+        self._head = (l1.weight.detach().to(torch.bfloat16).contiguous(),
+                      l1.bias.detach().float().contiguous(),
+                      l2.weight.detach().float().reshape(-1).contiguous(),
+                      l2.bias.detach().float().reshape(1).contiguous(),
+                      l1.weight.device)
 
     @staticmethod
     def sequence_info(batch: dict, device) -> tuple[torch.Tensor, int]:
@@ -220,17 +232,31 @@ class CTRModel(nn.Module):
         cu, max_len = self.sequence_info(batch, dev)
         x = self.rep_encoder(batch)
         h, _ = self.seq_encoder(x, {"cu_seqlens": cu, "max_seqlen": max_len})
-        return self.head(h), None
+        logits, _ = self.head(h, want_probs=False)
+        return logits.reshape(-1, 1), None
 
-    def head(self, h: torch.Tensor) -> torch.Tensor:
-        """Logits [T, 1]: the MLP head, clamped to +-15 (baseline/infer.py:437)."""
-        return torch.clamp(self.linear(h), min=-15.0, max=15.0)
+    @torch.no_grad()
+    def head(self, h: torch.Tensor, want_logits: bool = True, want_probs: bool = True):
+        """The MLP head, clamped to +-15 (baseline/infer.py:437), and the
+        sigmoid of predict (:686), in one launch (cti_ctr_head): returns
+        (logits [T] fp32 or None, probabilities [T] fp32 or None)."""
+        if getattr(self, "_head", None) is None or self._head[4] != self.linear[0].weight.device:
+            self._prepare_head()
+        w1, b1, w2, b2, _ = self._head
+        return ops.ctr_head(h.reshape(-1, self.d_model), w1, b1, w2, b2, 15.0,
+                            want_logits=want_logits, want_probs=want_probs)
+
+    def _probs(self, batch: dict) -> torch.Tensor:
+        dev = self.linear[0].weight.device
+        cu, max_len = self.sequence_info(batch, dev)
+        x = self.rep_encoder(batch)
+        h, _ = self.seq_encoder(x, {"cu_seqlens": cu, "max_seqlen": max_len})
+        return self.head(h, want_logits=False)[1]
 
     @torch.no_grad()
     def predict(self, batch: dict) -> torch.Tensor:
         """CTR probabilities [T] (fp32)."""
-        logits, _ = self.forward(batch)
-        return torch.sigmoid(logits.float()).reshape(-1)
+        return self._probs(batch)
 
     @torch.no_grad()
     def predict_host(self, batch: dict, chunks: int = 8,
@@ -316,8 +342,7 @@ class CTRModel(nn.Module):
             sub = {"_flat_values": vals_d[v0:vp], "_flat_row_offsets": ro_g.view(-1),
                    "_val_offsets": small_d[gi * F:(gi + 1) * F], "user_offsets": cu,
                    "max_seqlen": int((uo_np[s0 + 1:s1 + 1] - uo_np[s0:s1]).max())}
-            logits, _ = self.forward(sub)
-            out[a:b].copy_(torch.sigmoid(logits.float()).reshape(-1), non_blocking=True)
+            out[a:b].copy_(self._probs(sub), non_blocking=True)
         return out
 
 

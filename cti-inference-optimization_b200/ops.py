@@ -290,3 +290,27 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         "cti_varlen_attention",
     )
     return out
+
+
+def ctr_head(h: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
+             b2: torch.Tensor, limit: float = 15.0, want_logits: bool = True,
+             want_probs: bool = True):
+    """The CTR head in one launch (cti_ctr_head): logits = clamp(w2 .
+    relu(W1 h + b1) + b2, +-limit) and probs = sigmoid(logits), fp32 [T].
+    h [T, D] bf16; w1 [Hd, D] bf16; b1 [Hd], w2 [Hd], b2 [1] fp32.  Returns
+    (logits or None, probs or None)."""
+    require_cuda(h, "h", torch.bfloat16)
+    require_cuda(w1, "W1", torch.bfloat16)
+    for name, t in (("b1", b1), ("w2", w2), ("b2", b2)):
+        require_cuda(t, name, torch.float32)
+    T, D = h.shape
+    Hd = w1.shape[0]
+    dev = h.device
+    logits = torch.empty(T, dtype=torch.float32, device=dev) if want_logits else None
+    probs = torch.empty(T, dtype=torch.float32, device=dev) if want_probs else None
+    check(
+        lib.cti_ctr_head(ptr(h), ptr(w1), ptr(b1), ptr(w2), ptr(b2), T, D, Hd, float(limit),
+                         ptr(logits), ptr(probs), ptr(status_word(dev)), stream_handle(dev)),
+        "cti_ctr_head",
+    )
+    return logits, probs

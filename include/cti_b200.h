@@ -186,11 +186,12 @@ int cti_moe_expert_ffn_fused_gather(const void* x_bf16, int64_t T, const int32_t
                                     int32_t* status, void* stream);
 
 /* The same on CTA pairs (thread-block clusters of two SMs, one
- * tcgen05.mma.cta_group::2 stream per pair, 256-row tiles): each SM holds
- * half of every weight chunk, so it streams half the weight bytes per FLOP,
- * and the weight slots are double-buffered.  D == 256 only; otherwise the
- * same arguments, shapes and results (within fp32 accumulation order:
- * every row's result is computed the same way, bit for bit). */
+ * tcgen05.mma.cta_group::2 stream per pair, 256-row tiles, every MMA
+ * 256 x 256 x 16): each SM holds half of every weight K slab, so it streams
+ * half the weight bytes per FLOP; d_ff goes in 256-wide chunks whose GELU'd
+ * hidden activation passes through shared memory.  D == 256 and
+ * F % 256 == 0 (CTI_ERR_UNSUPPORTED otherwise); otherwise the same
+ * arguments, shapes and results. */
 int cti_moe_expert_ffn_fused_pair(const void* Xp_bf16, const void* W1_bf16, const float* b1,
                                   const void* W2_bf16, const float* b2,
                                   const int32_t* group_offsets, int G, int Gw,
@@ -198,7 +199,7 @@ int cti_moe_expert_ffn_fused_pair(const void* Xp_bf16, const void* W1_bf16, cons
                                   int32_t* status, void* stream);
 
 /* 1 if the fused kernels take this shape (D in {128, 256}, F % 128 == 0,
- * F <= 1024, G <= 256 groups, rows_total < 2^31 - 256), else 0. */
+ * F <= 1024, G <= 128 groups, rows_total < 2^31 - 256), else 0. */
 int cti_moe_expert_ffn_fused_supported(int D, int F, int G, int64_t rows_total);
 
 /* ------------------------------------------------------------------------
@@ -303,6 +304,21 @@ int cti_varlen_attention(const void* q_bf16, const void* k_bf16, const void* v_b
 int cti_add_layernorm(const void* x_bf16, const void* residual_bf16, const void* gamma_bf16,
                       const void* beta_bf16, int64_t rows, int cols, float eps, void* sum_bf16,
                       void* out_bf16, void* stream);
+
+/* ----------------------------------------------------------------------
+ * The CTR head in one launch: the configuration's MLP head, then the clamp
+ * and sigmoid of the reference head.  Replaces final_linear_clamp_kernel
+ * (online_best/infer.py:861-887, launched at :2529-2567) and the separate
+ * Linear / ReLU / Linear / clamp / sigmoid launches.
+ *   logits[t] = clamp(w2 . relu(W1 h[t] + b1) + b2, -limit, limit)
+ *   probs[t]  = 1 / (1 + exp(-logits[t]))
+ * h [T, D] bf16, W1 [Hd, D] bf16, b1 [Hd], w2 [Hd], b2 [1] fp32; the hidden
+ * activation stays in fp32 on chip.  logits / probs fp32 [T], either may be
+ * NULL (not both).  D % 64 == 0, D <= 256, Hd % 32 == 0, Hd <= 128.
+ * ---------------------------------------------------------------------- */
+int cti_ctr_head(const void* h_bf16, const void* W1_bf16, const float* b1, const float* w2,
+                 const float* b2, int64_t T, int D, int Hd, float limit, float* logits,
+                 float* probs, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }
