@@ -71,6 +71,16 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def ncu_traffic(kernel_key: str):
+    """DRAM bytes per launch of a kernel from its committed ncu capture
+    (profiles/dram_traffic.json), or None."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    try:
+        return json.loads(p.read_text())[kernel_key]["traffic_bytes"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def stage_bandwidths(stages_ms: dict, T: int, D: int, E: int, hbm_gbs: float) -> dict:
     """Algorithmic HBM bytes of the layer's memory-bound stages (bf16 rows,
     int32 indices, fp32 gates, 128-token router blocks) over their stage
@@ -484,7 +494,11 @@ def run_ours(args, world, rank, local):
         "roofline": {"bound": "tensor", "kernel": kernel_names[dom],
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": f"bf16_tflops of {peak_src}",
-                     "flops_per_launch": dom_flops, "traffic": None},
+                     "flops_per_launch": dom_flops,
+                     "traffic": ncu_traffic("fused_ffn_kernel<256> cfg2") if dom == "ffn_fused"
+                     else None,
+                     "traffic_source": "profiles/dram_traffic.json (one ncu capture of a "
+                                       "launch of this workload)"},
         "layer_roofline_frac": (2 * gemm_flops * world / (step_ms / 1e3) / 1e12 / world) / peak,
         "stages_ms": stages,
         "stages_hbm": stage_bandwidths(stages, T, cfg.d_model, cfg.num_experts,
