@@ -82,7 +82,11 @@ SIGNATURES = {
     ),
     "cti_selftest_wait_timeout": (_I, [_P, _I64, _P]),
     "cti_ctr_head": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, ctypes.c_float, _P, _P, _P, _P]),
-    "cti_varlen_attention": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _I, _I, _I, _I, _P, _P]),
+    "cti_rep_encoder_fused": (
+        _I, [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _P, _P, _P, _I, ctypes.c_float, _P,
+             _P, _P]),
+    "cti_varlen_attention": (
+        _I, [_P, _P, _P, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _I, _P, _P, _P]),
     "cti_add_layernorm": (
         _I,
         [_P, _P, _P, _P, _I64, _I, ctypes.c_float, _P, _P, _P],

@@ -28,12 +28,6 @@ constexpr float C0 = -0.9999869465827942f, C1 = -1.1513246297836304f,
 constexpr float kU0 = 6.0f;
 }  // namespace gelu_detail
 
-CTI_DEVICE float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // In-place GELU of N values (N even), ordered so that the N/2 packed Horner
 // chains interleave: every step issues N/2 independent f32x2 FMAs.
 // Infinite inputs give NaN.

@@ -25,10 +25,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // 2-D bf16 row-major matrix [rows, cols] (cols contiguous), loaded as boxes
-// of box_cols x box_rows with the 128-byte swizzle (box_cols * 2 == 128).
+// of box_cols x box_rows with the 128-byte swizzle (box_cols * 2 == 128), or
+// the 64-byte swizzle (box_cols * 2 == 64) when `swizzle` says so.
 // Out-of-range rows read as zero.
 inline bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                              uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols) {
+                              uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols,
+                              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
@@ -38,7 +40,7 @@ inline bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows,
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }

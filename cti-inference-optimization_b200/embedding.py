@@ -76,10 +76,51 @@ class RepEncoder(nn.Module):
         return ops.embedding_bag_sum(v, o, vo, table.detach(), self.table_row_base, self.vocab,
                                      self.slot_num, out_dtype=out_dtype)
 
+    def fused_supported(self) -> bool:
+        """Whether forward() takes the one-launch path (cti_rep_encoder_fused):
+        64-wide fp16 tables, bf16 LayerNorm and Linear, d_model 128 or 256."""
+        w = self.linear.weight
+        return (self.emb_dim == 64 and w.is_cuda and w.dtype == torch.bfloat16
+                and self.emb.weight.dtype == torch.float16 and w.shape[0] in (128, 256)
+                and self.input_norm.weight.dtype == torch.bfloat16)
+
+    @torch.no_grad()
+    def fused_params(self):
+        """(Wg bf16 [N, F*64] = W * gamma, r1 fp32 [N] = row sums of Wg,
+        c fp32 [N] = W beta + b): the LayerNorm folded into the Linear,
+        rebuilt when a parameter changes."""
+        key = tuple((p.data_ptr(), p._version) for p in
+                    (self.linear.weight, self.linear.bias, self.input_norm.weight,
+                     self.input_norm.bias))
+        cache = getattr(self, "_fused", None)
+        if cache is None or cache[0] != key:
+            W = self.linear.weight.float()
+            wg = (W * self.input_norm.weight.float()[None, :]).to(torch.bfloat16).contiguous()
+            r1 = wg.float().sum(1).contiguous()
+            c = (W @ self.input_norm.bias.float() + self.linear.bias.float()).contiguous()
+            cache = (key, wg, r1, c)
+            self._fused = cache
+        return cache[1], cache[2], cache[3]
+
     def forward(self, batch: dict) -> torch.Tensor:
         """linear(input_norm(pooled)) in bf16 (the model after
-        prepare_for_inference); the LayerNorm runs on the sm_100a kernel,
-        which raises for other dtypes."""
+        prepare_for_inference).  Supported shapes run as one sm_100a launch
+        (pooling, LayerNorm folded into the Linear, never writing the pooled
+        rows); others pool, normalise on the LayerNorm kernel (which raises
+        for widths it does not cover) and multiply on cuBLAS."""
+        if self.fused_supported():
+            dev = self.emb.weight.device
+            if "_flat_values" not in batch:
+                v, o, vo = flatten_slot_batch(batch, self.slot_num)
+            else:
+                v, o, vo = batch["_flat_values"], batch["_flat_row_offsets"], batch["_val_offsets"]
+            v = v.to(dev, torch.int64, non_blocking=True).contiguous()
+            o = o.to(dev, torch.int64, non_blocking=True).contiguous()
+            vo = vo.to(dev, torch.int64, non_blocking=True).contiguous()
+            wg, r1, c = self.fused_params()
+            return ops.rep_encoder_fused(v, o, vo, self.emb.weight.detach(), self.table_row_base,
+                                         self.vocab, self.slot_num, wg, r1, c,
+                                         self.input_norm.eps)
         pooled = self.pool(batch, out_dtype=self.input_norm.weight.dtype)
         _, normed = ops.add_layernorm(pooled, None, self.input_norm.weight,
                                       self.input_norm.bias, self.input_norm.eps)

@@ -244,6 +244,45 @@ def embedding_bag_sum(
     return out
 
 
+def rep_encoder_fused(values: torch.Tensor, row_offsets: torch.Tensor, val_offsets: torch.Tensor,
+                      table: torch.Tensor, table_row_base: torch.Tensor, vocab: torch.Tensor,
+                      num_features: int, wg: torch.Tensor, r1: torch.Tensor, c: torch.Tensor,
+                      eps: float = 1e-5, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The RepEncoder in one launch (cti_rep_encoder_fused): the embedding-bag
+    pooling of ``embedding_bag_sum`` (64-wide fp16 rows), LayerNorm over the
+    pooled row and the Linear, with the LayerNorm folded into the weights:
+    ``wg`` bf16 [N, F*64] = W * gamma, ``r1`` fp32 [N] = wg.float().sum(1),
+    ``c`` fp32 [N] = W beta + b.  Returns bf16 [B, N]; N in {128, 256}."""
+    for name, t in (("values", values), ("row_offsets", row_offsets),
+                    ("val_offsets", val_offsets), ("table_row_base", table_row_base),
+                    ("vocab", vocab)):
+        require_cuda(t, name, torch.int64)
+    require_cuda(table, "table", torch.float16)
+    require_cuda(wg, "wg", torch.bfloat16)
+    require_cuda(r1, "r1", torch.float32)
+    require_cuda(c, "c", torch.float32)
+    F = num_features
+    if row_offsets.numel() % F != 0:
+        raise ValueError("row_offsets length must be a multiple of the feature count")
+    B = row_offsets.numel() // F - 1
+    dim = table.shape[1]
+    N = wg.shape[0]
+    if wg.shape[1] != F * dim or r1.numel() != N or c.numel() != N:
+        raise ValueError("wg must be [N, F*dim] with r1, c of length N")
+    dev = table.device
+    if out is None:
+        out = torch.empty((B, N), dtype=torch.bfloat16, device=dev)
+    check(
+        lib.cti_rep_encoder_fused(
+            ptr(values), values.numel(), ptr(row_offsets), ptr(val_offsets),
+            ptr(table_row_base), ptr(vocab), ptr(table), table.shape[0], B, F, dim, ptr(wg),
+            ptr(r1), ptr(c), N, float(eps), ptr(out), ptr(status_word(dev)), stream_handle(dev),
+        ),
+        "cti_rep_encoder_fused",
+    )
+    return out
+
+
 def add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor,
                   bias: torch.Tensor, eps: float = 1e-5, write_sum: bool = True):
     """The CTR model's residual add + LayerNorm: s = x + residual (bf16), out =
@@ -285,8 +324,9 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     out = torch.empty((T, H, hd), dtype=torch.bfloat16, device=q.device)
     check(
         lib.cti_varlen_attention(ptr(q), ptr(k), ptr(v), q.stride(0), k.stride(0), v.stride(0),
-                                 ptr(cu_seqlens), cu_seqlens.numel() - 1, int(max_seqlen), H, hd,
-                                 ptr(out), stream_handle(q.device)),
+                                 ptr(cu_seqlens), cu_seqlens.numel() - 1, int(max_seqlen), T, H,
+                                 hd, ptr(out), ptr(status_word(q.device)),
+                                 stream_handle(q.device)),
         "cti_varlen_attention",
     )
     return out

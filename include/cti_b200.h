@@ -273,20 +273,47 @@ int cti_embbag_sum(const int64_t* values, int64_t n_values, const int64_t* row_o
                    int F, int dim, void* out, int out_dtype, int32_t* status, void* stream);
 
 /* ----------------------------------------------------------------------
+ * The RepEncoder in one launch: embedding-bag pooling (as cti_embbag_sum,
+ * dim 64, bf16-rounded sums), LayerNorm over the F*64 pooled columns and the
+ * Linear to N = d_model, never writing the pooled rows
+ * (baseline/infer.py:253-265 RepEncoder.forward; online_best/infer.py:793-827,
+ * :829-858 and :1061-1085, the pooling, LayerNorm and Linear launches).  The
+ * LayerNorm is folded into the weights by the caller:
+ *   wg bf16 [N, F*64] = W * gamma;  r1 fp32 [N] = sum_k wg[n, k];
+ *   c fp32 [N] = W beta + b;
+ *   out[b, n] = rstd_b * (sum_k wg[n, k] x[b, k] - mean_b * r1[n]) + c[n]
+ * with mean_b, rstd_b = 1/sqrt(var_b + eps) over the bf16 pooled row x[b].
+ * Batch layout, clamping and bounds errors as cti_embbag_sum.  out bf16
+ * [B, N] contiguous (16-byte aligned).  dim 64 and N in {128, 256} only
+ * (CTI_ERR_UNSUPPORTED otherwise).
+ * ---------------------------------------------------------------------- */
+int cti_rep_encoder_fused(const int64_t* values, int64_t n_values, const int64_t* row_offsets,
+                          const int64_t* val_offsets, const int64_t* table_row_base,
+                          const int64_t* vocab, const void* table_f16, int64_t table_rows,
+                          int64_t B, int F, int dim, const void* wg_bf16, const float* r1,
+                          const float* c, int N, float eps, void* out_bf16, int32_t* status,
+                          void* stream);
+
+/* ----------------------------------------------------------------------
  * Causal attention inside packed variable-length sequences (the CTR model's
  * per-layer attention: baseline/infer.py:267-276 scaled_dot_product with the
  * sequence causal mask of :420-427; online_best/infer.py:1132-1202).
  *   out[t, h, :] = softmax over the keys j of t's sequence with j <= t of
  *                  q[t,h,:].k[j,h,:] / sqrt(head_dim), applied to v[j,h,:]
- * q, k, v: bf16 [T][heads][head_dim] views with token strides (elements,
- * multiples of 8, >= heads*head_dim); cu_seqlens int32 [num_seqs+1] token
- * offsets; out bf16 [T][heads][head_dim] contiguous.  head_dim 32 only
- * (CTI_ERR_UNSUPPORTED otherwise); any sequence length up to max_seqlen.
+ * q, k, v: bf16 [tokens][heads][head_dim] views with token strides
+ * (elements, multiples of 8, >= heads*head_dim; 16-byte aligned bases);
+ * cu_seqlens int32 [num_seqs+1] non-decreasing token offsets, cu[0] >= 0;
+ * out bf16 [tokens][heads][head_dim] contiguous, written for the tokens
+ * [cu[0], min(cu[num_seqs], tokens)) only.  head_dim 32 only
+ * (CTI_ERR_UNSUPPORTED otherwise).  Sequences of any length; max_seqlen is
+ * the caller's bound (checked >= 0, not needed by the kernel).  `status`
+ * (int32[2], may be NULL) receives CTI_ERR_TIMEOUT if a pipeline wait runs
+ * out, CTI_ERR_INVALID_ARG if cu[0] < 0.
  * ---------------------------------------------------------------------- */
 int cti_varlen_attention(const void* q_bf16, const void* k_bf16, const void* v_bf16,
                          int64_t q_stride, int64_t k_stride, int64_t v_stride,
-                         const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int heads,
-                         int head_dim, void* out_bf16, void* stream);
+                         const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int64_t tokens,
+                         int heads, int head_dim, void* out_bf16, int32_t* status, void* stream);
 
 /* ----------------------------------------------------------------------
  * Residual add + LayerNorm of the CTR model around the MoE layer: the

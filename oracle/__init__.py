@@ -13,10 +13,12 @@ Contents:
   embbag_ref.py      restatement of the reference embedding-bag pooling
                      (baseline/infer.py:253-263) in fp32 on CPU.
   router_order.c     the router restated in C with the kernel's fixed
-                     reduction order (one fmaf chain per logit), for a
-                     strict bit-exact check of expert indices.
+                     reduction order (two fmaf chains per logit, even and
+                     odd d, then the bias), for a strict bit-exact check
+                     of expert indices.
   e2e_ref.py         the reference CTR model graph (baseline/infer.py:
-                     244-439) in fp32 at the end-to-end configuration.
+                     244-439) in fp32 at the end-to-end configuration,
+                     and its RepEncoder alone (rep_encoder_ref, :253-265).
   build.py           compiles router_order.c into _build/liborder.so.
 
 Pinning: tests/golden/ holds fixtures produced by running the reference's

@@ -45,6 +45,27 @@ def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return out
 
 
+def rep_encoder_ref(sd: dict, batch: dict, *, slot_num: int, table_row_base=None,
+                    vocab=None) -> torch.Tensor:
+    """RepEncoder.forward (baseline/infer.py:253-265): the sum pooling of
+    every (sample, slot) bag, LayerNorm over the slot_num * emb_dim pooled
+    columns, Linear to d_model; fp32 [B, d_model].  ``sd`` holds the
+    ``rep_encoder.*`` parameters under the reference's names."""
+    # The embedding table stays in its own dtype: the pooling upcasts only
+    # the rows it gathers.
+    g = {k: v.float() for k, v in sd.items()
+         if k.startswith("rep_encoder.") and k != "rep_encoder.emb.weight"}
+    table = sd["rep_encoder.emb.weight"]
+    if table_row_base is None:  # one shared table, as in the reference
+        table_row_base = torch.zeros(slot_num, dtype=torch.int64)
+        vocab = torch.full((slot_num,), table.shape[0], dtype=torch.int64)
+    pooled = embbag_ref(batch["_flat_values"], batch["_flat_row_offsets"], batch["_val_offsets"],
+                        table, table_row_base, vocab, slot_num)
+    x = F.layer_norm(pooled, (pooled.shape[1],), g["rep_encoder.input_norm.weight"],
+                     g["rep_encoder.input_norm.bias"])
+    return F.linear(x, g["rep_encoder.linear.weight"], g["rep_encoder.linear.bias"])
+
+
 def ctr_forward_ref(sd: dict, batch: dict, *, slot_num: int, n_heads: int, num_layers: int,
                     num_experts: int, table_row_base=None, vocab=None, force_routes=None,
                     routing: list | None = None):
@@ -56,18 +77,8 @@ def ctr_forward_ref(sd: dict, batch: dict, *, slot_num: int, n_heads: int, num_l
     (the gate's own top-2 [T, 2] on this run's activations, the fp64 gap
     [T] between its top-1/top-2 or top-2/top-3 logits, whichever is
     smaller)."""
-    # The embedding table stays in its own dtype: the pooling upcasts only
-    # the rows it gathers.
     g = {k: v.float() for k, v in sd.items() if k != "rep_encoder.emb.weight"}
-    table = sd["rep_encoder.emb.weight"]
-    if table_row_base is None:  # one shared table, as in the reference
-        table_row_base = torch.zeros(slot_num, dtype=torch.int64)
-        vocab = torch.full((slot_num,), table.shape[0], dtype=torch.int64)
-    pooled = embbag_ref(batch["_flat_values"], batch["_flat_row_offsets"], batch["_val_offsets"],
-                        table, table_row_base, vocab, slot_num)
-    x = F.layer_norm(pooled, (pooled.shape[1],), g["rep_encoder.input_norm.weight"],
-                     g["rep_encoder.input_norm.bias"])
-    x = F.linear(x, g["rep_encoder.linear.weight"], g["rep_encoder.linear.bias"])
+    x = rep_encoder_ref(sd, batch, slot_num=slot_num, table_row_base=table_row_base, vocab=vocab)
     T, D = x.shape
     hd = D // n_heads
     for i in range(num_layers):
