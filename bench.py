@@ -471,6 +471,8 @@ def run_ours(args, world, rank, local):
                                           "chunks": r4["chunks"]},
                      "stages_ms": r4["stages_ms"], "tokens_per_s": r4["tokens_per_s"],
                      "expert_ffn_roofline": r4["roofline"], "pooling": r4["pooling"],
+                     "rep_encoder": r4["rep_encoder"],
+                     "attention_kernel": r4["attention_kernel"],
                      "steps": E2E_MODEL_STEPS, "warmup": EP_WARMUP}
 
     if rank != 0:
@@ -780,7 +782,7 @@ def measure_e2e_model(args, world, rank, local, flush, steps: int, warmup: int,
 
     # Stage split of one forward (CUDA events), median of 3.
     enc = model.seq_encoder
-    stage = {"pool": [], "rep_norm_linear": [], "attention": [], "moe": [], "head": []}
+    stage = {"rep_encoder": [], "attention": [], "moe": [], "head": []}
     for _ in range(3):
         flush.zero_()
         evs = []
@@ -791,12 +793,8 @@ def measure_e2e_model(args, world, rank, local, flush, steps: int, warmup: int,
             evs.append((name, e))
 
         mark("start")
-        pooled = model.rep_encoder.pool(batch, out_dtype=torch.bfloat16)
-        mark("pool")
-        _, normed = ops.add_layernorm(pooled, None, model.rep_encoder.input_norm.weight,
-                                      model.rep_encoder.input_norm.bias)
-        x = model.rep_encoder.linear(normed)
-        mark("rep_norm_linear")
+        x = model.rep_encoder(batch)
+        mark("rep_encoder")
         cu = batch["user_offsets"].to(torch.int32)
         h, _ = enc(x, {"cu_seqlens": cu, "max_seqlen": 256, "mark": mark})
         model.head(h)
@@ -823,10 +821,31 @@ def measure_e2e_model(args, world, rank, local, flush, steps: int, warmup: int,
     ffn_flops = 4.0 * (2 * T) * enc.d_model * moe0.dim_ff
     peaks, peak_src = load_peaks()
     ffn_tflops = ffn_flops / (ffn_ms / 1e3) / 1e12
-    # The pooling, against HBM (algorithmic bytes; Zipf ids re-hit rows in L2).
+    # The RepEncoder: the model's path (the stage above: pooling kernel
+    # writing [T, 1792] bf16, LayerNorm kernel, cuBLAS Linear) against the
+    # fused kernel timed alone; and the pooling kernel against HBM
+    # (algorithmic bytes; Zipf ids re-hit rows in L2).
+    rep = model.rep_encoder
+    pool = lambda: rep.pool(batch, out_dtype=torch.bfloat16)
+    pool()
+    pool_ms = statistics.median(time_steps(pool, 3, flush, dev))
+
+    fused = lambda: rep.forward_fused(batch)
+    fused()
+    fused_ms = statistics.median(time_steps(fused, 3, flush, dev))
     N = bb.values.numel()
     pool_bytes = 8 * N + 8 * 28 * (T + 1) + 128 * N + 2 * T * 28 * 64
-    pool_gbs = pool_bytes / (stages["pool"] / 1e3) / 1e9
+    pool_gbs = pool_bytes / (pool_ms / 1e3) / 1e9
+    # The attention kernel alone on layer 0's q, k, v of this batch, times the
+    # layer count (the "attention" stage also holds the qkv and output
+    # projections and the two add + LayerNorm launches).
+    layer0 = enc.norm1[0]
+    _, h0 = ops.add_layernorm(x0, None, layer0.weight, layer0.bias, layer0.eps)
+    qkv0 = torch.nn.functional.linear(h0, *enc._qkv[0]).view(T, 3, enc.n_heads, enc.head_dim)
+    cu0 = batch["user_offsets"].to(torch.int32)
+    att = lambda: ops.varlen_attention(qkv0[:, 0], qkv0[:, 1], qkv0[:, 2], cu0, 256)
+    att()
+    att_ms = statistics.median(time_steps(att, 5, flush, dev))
     cpu = None
     if rank == 0 and cpu_seconds > 0:
         cpu = cpu_baseline_e2e(model, bb, uo, cpu_seconds)
@@ -840,12 +859,22 @@ def measure_e2e_model(args, world, rank, local, flush, steps: int, warmup: int,
                      "unit": "TFLOP/s", "frac": ffn_tflops / float(peaks["bf16_tflops"]),
                      "peak_source": f"bf16_tflops of {peak_src}", "flops_per_launch": ffn_flops,
                      "ms_per_launch": ffn_ms, "traffic": None},
-        "pooling": {"kernel": "embbag_kernel<64, bf16>", "algorithmic_gbs": pool_gbs,
-                    "bytes_per_launch": pool_bytes,
+        "pooling": {"kernel": "embbag_kernel<64, bf16>", "ms": pool_ms,
+                    "algorithmic_gbs": pool_gbs, "bytes_per_launch": pool_bytes,
                     "note": "algorithmic bytes (128 B per id) over time; Zipf ids re-hit rows "
                             "in L2, so this exceeds the HBM copy bandwidth"},
+        "rep_encoder": {"stage_ms": stages["rep_encoder"],
+                        "path": "pooling kernel -> [T, 1792] bf16 -> LayerNorm kernel -> "
+                                "cuBLAS Linear",
+                        "fused_ms": fused_ms,
+                        "fused": "cti_rep_encoder_fused, timed alone (pooling, LayerNorm "
+                                 "folded into the Linear, no [T, 1792] in HBM)"},
+        "attention_kernel": {"ms_per_layer": att_ms, "ms_per_batch": att_ms * enc.num_layers,
+                             "kernel": "varlen_attention_kernel (tcgen05)"},
         "stages_ms": stages, "tokens_per_s": T / (step_ms / 1e3),
-        "launches_per_batch": 2 + 7 * enc.num_layers, "clocks": clocks, "cpu_baseline": cpu,
+        # Ours per batch: pooling and LayerNorm, per layer 2 add + LayerNorm,
+        # the attention and the MoE chain of 5, and the head.
+        "launches_per_batch": 3 + 8 * enc.num_layers, "clocks": clocks, "cpu_baseline": cpu,
     }
     del model, batch, pinned
     torch.cuda.empty_cache()
@@ -885,6 +914,7 @@ def run_e2e(args, world, rank, local):
                 "h2d_bytes_per_step": r["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": r["d2h_bytes_per_step"], "chunks": r["chunks"]},
         "roofline": r["roofline"], "pooling": r["pooling"], "stages_ms": r["stages_ms"],
+        "rep_encoder": r["rep_encoder"], "attention_kernel": r["attention_kernel"],
         "tokens_per_s": r["tokens_per_s"],
         "gpu_launches": r["launches_per_batch"] * args.steps,
         "clocks": r["clocks"], "cpu_baseline": r["cpu_baseline"],
@@ -896,6 +926,7 @@ def cpu_baseline_e2e(model, bb, uo, seconds: float, sample_seqs: int = 2):
     """The oracle (fp32 CPU restatement of the reference model) on the first
     `sample_seqs` sequences of the batch, scaled to the whole batch by
     tokens."""
+    from cti_b200 import synth
     from oracle import e2e_ref
 
     torch.set_num_threads(os.cpu_count() or 1)

@@ -52,7 +52,7 @@ def test_fused_rep_encoder_matches_oracle(cuda_device, B, d_model):
     bb = synth.bag_batch(batch=B, seed=B, vocab_hi=2e5, lam_hi=50.0)
     enc = _encoder(cuda_device, bb, d_model, seed=B)
     assert enc.fused_supported()
-    out = enc(_batch(bb))
+    out = enc.forward_fused(_batch(bb))
     _lib.raise_on_status(cuda_device)
     assert out.shape == (B, d_model) and out.dtype == torch.bfloat16
     sd = {"rep_encoder." + k: v.detach().cpu() for k, v in enc.state_dict().items()}
@@ -62,16 +62,13 @@ def test_fused_rep_encoder_matches_oracle(cuda_device, B, d_model):
 
 
 def test_fused_rep_encoder_matches_unfused_path(cuda_device):
-    from cti_b200 import _lib, ops, synth
+    from cti_b200 import _lib, synth
 
     bb = synth.bag_batch(batch=2000, seed=7, vocab_hi=2e5, lam_hi=50.0)
     enc = _encoder(cuda_device, bb, 256, seed=7)
     batch = {k: v.to(cuda_device) for k, v in _batch(bb).items()}
-    fused = enc(batch)
-    pooled = enc.pool(batch, out_dtype=torch.bfloat16)
-    _, normed = ops.add_layernorm(pooled, None, enc.input_norm.weight, enc.input_norm.bias,
-                                  enc.input_norm.eps)
-    unfused = enc.linear(normed)
+    fused = enc.forward_fused(batch)
+    unfused = enc(batch)
     _lib.raise_on_status(cuda_device)
     assert _rel(fused, unfused) < 1e-2
 
