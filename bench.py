@@ -983,6 +983,20 @@ def run_profile_workload(args):
         _lib.raise_on_status(dev)
         print(f"profile workload embbag: {bb.values.numel()} ids")
         return
+    if args.profile == "attention":
+        # Configuration 4's attention: 2048 packed sequences U{16..256}, 8
+        # heads of 32, q/k/v the thirds of one [T, 768] projection output.
+        lens = synth.packed_lengths(synth.CFG4_SAMPLES, 16, 256, 0)
+        cu = synth.cu_seqlens(lens).to(dev)
+        T = int(lens.sum())
+        g = torch.Generator(device=dev).manual_seed(0)
+        qkv = torch.randn(T, 768, generator=g, device=dev).bfloat16().view(T, 3, 8, 32)
+        for _ in range(args.warmup + args.steps):
+            ops.varlen_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, 256)
+        torch.cuda.synchronize(dev)
+        _lib.raise_on_status(dev)
+        print(f"profile workload attention: T={T}, {args.warmup + args.steps} launches")
+        return
     cfg = synth.CFG2
     T, _ = synth.moe_tokens(cfg)
     w = synth.moe_weights(cfg.d_model, cfg.num_experts, cfg.dim_ff, cfg.zipf_bias, device=dev)
@@ -1107,8 +1121,8 @@ def main():
                     help="cfg5 rows exchange: overlapped point-to-point or plain all_to_all")
     ap.add_argument("--profile", default=None,
                     choices=["router", "dispatch", "ffn_fused", "ffn_gather", "ffn_fc1", "combine",
-                             "layer", "embbag"],
-                    help="run one stage of the configuration-2 workload for an ncu capture")
+                             "layer", "embbag", "attention"],
+                    help="run one stage of the configuration-2 workload (attention: of configuration 4) for an ncu capture")
     args = ap.parse_args()
     if args.profile:
         run_profile_workload(args)

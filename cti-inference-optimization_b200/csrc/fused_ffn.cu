@@ -24,13 +24,15 @@
 // left the tensor core idle during every wait: the issue queue holds only a
 // few MMAs).  After the last chunk, acc2 + b2 is written to Y as bf16.
 //
-// Roles (608 threads; 640 with the row gather below): warp 0 TMA producer
-// (X tile once per tile unless warp 19 gathers it; W1 and W2 chunks through
-// two rings of whole-chunk slots), warp 1 TMEM owner and GEMM1 issuer
-// (tcgen05.mma M=128, N=128, K=16, bf16 -> fp32), warps 2-17 epilogue (four
-// warps per TMEM lane quadrant, each owning 32 of a chunk's 128 columns and
-// a quarter of the output columns; the expert's biases are staged in shared
-// memory once per expert change), warp 18 GEMM2 issuer (N=D, A from TMEM).
+// Roles (640 threads; 672 with the row gather below): warp 0 TMA producer of
+// the X tile (once per tile, unless warp 20 gathers it) and of W1 in
+// half-chunk slots ([128 x D/2], a 3-slot ring), warp 1 TMEM owner and GEMM1
+// issuer (tcgen05.mma M=128, N=128, K=16, bf16 -> fp32), warps 2-17 epilogue
+// (four warps per TMEM lane quadrant, each owning 32 of a chunk's 128 columns
+// and a quarter of the output columns; biases read through the read-only
+// cache, the next chunk's prefetched before the accumulator wait), warp 18
+// GEMM2 issuer (N=D, A from TMEM), warp 19 TMA producer of W2 in half-chunk
+// slots ([D x 64], a 2-slot ring).
 //
 // TMEM: acc2 in columns [0, D), acc1 buffers at 256 and 384 (512 allocated).
 // The epilogue produces H(c) in two halves (chunk columns [0, 64) and
@@ -39,9 +41,8 @@
 // fp32 columns [64h + 16s, +16) of each half h and writes their 16 bf16
 // values to the first 8 of those columns, so the 16-wide K step k of GEMM2
 // reads 8 contiguous columns at 64*(k/4) + 16*(k%4).
-// Shared memory: X tile (D/64 slabs of 16 KB) + one W1 and one W2 slot of
-// 64 KB each for D=256 (two of 32 KB each for D=128) + biases 5 KB +
-// scheduler 2 KB.
+// Shared memory: X tile (D/64 slabs of 16 KB) + three W1 and two W2
+// half-chunk slots (32 KB each at D=256) + scheduler 2 KB.
 // d_ff <= 1024 (one expert's b1 in shared memory).
 #include "common.cuh"
 #include "gelu.cuh"
