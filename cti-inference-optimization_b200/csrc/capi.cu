@@ -4,6 +4,8 @@
 // the same layer between host buffers, pipelined over token chunks.
 #include <cstring>
 
+#include <vector>
+
 #include "common.cuh"
 #include "tmap.cuh"
 
@@ -177,7 +179,10 @@ extern "C" int cti_moe_layer_forward_host(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaStream_t s_in = static_cast<cudaStream_t>(copy_stream_in);
   cudaStream_t s_out = static_cast<cudaStream_t>(copy_stream_out);
-  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // start, in, out
+  const int64_t nchunks = (T + chunk - 1) / chunk;
+  if (nchunks > 4096) return CTI_ERR_UNSUPPORTED;
+  // ev[0] start, ev[1] out (reused per chunk), ev[2 + i] chunk i copied in.
+  std::vector<cudaEvent_t> ev((size_t)nchunks + 2, nullptr);
   for (auto& e : ev)
     if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
       for (auto& d : ev)
@@ -193,27 +198,40 @@ extern "C" int cti_moe_layer_forward_host(
   // The copies start after everything already enqueued on `stream`.
   if (cuda_ok(cudaEventRecord(ev[0], s)) && cuda_ok(cudaStreamWaitEvent(s_in, ev[0], 0)))
     cuda_ok(cudaStreamWaitEvent(s_out, ev[0], 0));
-  for (int64_t t0 = 0; rc == CTI_OK && t0 < T; t0 += chunk) {
+  // Every chunk's copy in first, so that the copy stream runs back to back
+  // whatever the host's launch rate for the layers below.
+  int64_t copied = 0;
+  for (int64_t i = 0; rc == CTI_OK && i < nchunks; ++i) {
+    const int64_t t0 = i * chunk;
+    const int64_t n = (T - t0) < chunk ? (T - t0) : chunk;
+    const size_t off = (size_t)t0 * row_bytes, bytes = (size_t)n * row_bytes;
+    if (!cuda_ok(cudaMemcpyAsync(static_cast<uint8_t*>(x_dev) + off,
+                                 static_cast<const uint8_t*>(x_host) + off, bytes,
+                                 cudaMemcpyHostToDevice, s_in)) ||
+        !cuda_ok(cudaEventRecord(ev[2 + i], s_in)))
+      break;
+    copied = i + 1;
+  }
+  for (int64_t i = 0; rc == CTI_OK && i < copied; ++i) {
+    const int64_t t0 = i * chunk;
     const int64_t n = (T - t0) < chunk ? (T - t0) : chunk;
     const size_t off = (size_t)t0 * row_bytes, bytes = (size_t)n * row_bytes;
     uint8_t* xd = static_cast<uint8_t*>(x_dev) + off;
     uint8_t* od = static_cast<uint8_t*>(out_dev) + off;
-    if (!cuda_ok(cudaMemcpyAsync(xd, static_cast<const uint8_t*>(x_host) + off, bytes,
-                                 cudaMemcpyHostToDevice, s_in)) ||
-        !cuda_ok(cudaEventRecord(ev[1], s_in)) || !cuda_ok(cudaStreamWaitEvent(s, ev[1], 0)))
-      break;
+    if (!cuda_ok(cudaStreamWaitEvent(s, ev[2 + i], 0))) break;
     rc = cti_moe_layer_forward(xd, wg, bg, W1_bf16, b1, W2_bf16, b2, n, D, E, F, act, renorm, od,
                                workspace, workspace_bytes, status, stream);
     if (rc != CTI_OK) break;
-    if (!cuda_ok(cudaEventRecord(ev[2], s)) || !cuda_ok(cudaStreamWaitEvent(s_out, ev[2], 0)))
+    if (!cuda_ok(cudaEventRecord(ev[1], s)) || !cuda_ok(cudaStreamWaitEvent(s_out, ev[1], 0)))
       break;
     cuda_ok(cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + off, od, bytes,
                             cudaMemcpyDeviceToHost, s_out));
   }
-  // `stream` resumes after the last copy back (also on an early error, so
-  // that nothing enqueued later races the copies already in flight).
-  if (cudaEventRecord(ev[2], s_out) == cudaSuccess) cudaStreamWaitEvent(s, ev[2], 0);
-  if (cudaEventRecord(ev[1], s_in) == cudaSuccess) cudaStreamWaitEvent(s, ev[1], 0);
+  // `stream` resumes after the last copy back and the last copy in (also on
+  // an early error, so that nothing enqueued later races the copies already
+  // in flight).
+  if (cudaEventRecord(ev[1], s_out) == cudaSuccess) cudaStreamWaitEvent(s, ev[1], 0);
+  if (cudaEventRecord(ev[0], s_in) == cudaSuccess) cudaStreamWaitEvent(s, ev[0], 0);
   for (auto& e : ev) cudaEventDestroy(e);
   return rc;
 }

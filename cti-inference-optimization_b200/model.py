@@ -264,9 +264,9 @@ class CTRModel(nn.Module):
         """``predict`` for a batch in host memory (the reference's flat layout,
         ``online_best/infer.py:742-779`` moves it to the GPU before the
         forward): the packed sequences are cut into ``chunks`` groups of
-        about equal token count, and the host->device copy of one group's
-        ids and offsets (a side stream) overlaps the forward of the group
-        before it.  Every sequence is computed independently (pooling and
+        about equal token count; every group's ids and offsets are copied
+        on a side stream first, and each group's forward starts as soon as
+        its own copies have landed, overlapping the later groups' copies.  Every sequence is computed independently (pooling and
         MoE per token, attention inside the sequence), so the chunks give
         the whole batch's probabilities; only the library GEMMs' choice of
         kernel may change with the row count, within rounding.
@@ -319,7 +319,10 @@ class CTRModel(nn.Module):
         s_in.wait_stream(s_comp)  # staging buffers are free once earlier work is done
         with torch.cuda.stream(s_in):
             small_d[:small_h.numel()].copy_(small_h, non_blocking=True)
+        # Every group's copies first, so that the copy stream runs back to
+        # back whatever the host's launch rate for the forwards below.
         vp = rp = 0
+        staged = []
         for gi, (s0, s1, a, b) in enumerate(groups):
             n = b - a
             v0, r0 = vp, rp
@@ -335,11 +338,15 @@ class CTRModel(nn.Module):
                     rp += n + 1
                 ready = torch.cuda.Event()
                 ready.record(s_in)
+            staged.append((v0, vp, r0, rp, ready))
+        for gi, (s0, s1, a, b) in enumerate(groups):
+            n = b - a
+            v0, v1, r0, r1, ready = staged[gi]
             s_comp.wait_event(ready)
-            ro_g = ro_d[r0:rp].view(F, n + 1)
+            ro_g = ro_d[r0:r1].view(F, n + 1)
             ro_g.sub_(ro_g[:, :1].clone())
             cu = small_d[cu_pos[gi]:cu_pos[gi] + s1 - s0 + 1]
-            sub = {"_flat_values": vals_d[v0:vp], "_flat_row_offsets": ro_g.view(-1),
+            sub = {"_flat_values": vals_d[v0:v1], "_flat_row_offsets": ro_g.view(-1),
                    "_val_offsets": small_d[gi * F:(gi + 1) * F], "user_offsets": cu,
                    "max_seqlen": int((uo_np[s0 + 1:s1 + 1] - uo_np[s0:s1]).max())}
             out[a:b].copy_(self._probs(sub), non_blocking=True)
