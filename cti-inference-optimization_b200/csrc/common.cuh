@@ -271,6 +271,20 @@ CTI_DEVICE void tmem_ld_32x32b_2x32_sync(uint32_t taddr_a, uint32_t taddr_b, uin
       : "memory");
 }
 
+// 32 bytes to global memory: one 256-bit store when p is 32-byte aligned,
+// else two 16-byte stores (p 16-byte aligned).
+CTI_DEVICE void st_global_32B(void* p, const uint32_t (&w)[8], bool aligned32) {
+  if (aligned32) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+  } else {
+    uint4* d = reinterpret_cast<uint4*>(p);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
 // 32 lanes x 32 consecutive 32-bit columns (store).
 CTI_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(

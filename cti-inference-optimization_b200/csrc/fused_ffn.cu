@@ -447,7 +447,6 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
     const int ew = warp - 2;           // 0..15
     const int q = warp & 3;            // TMEM lane quadrant of this warp
     const int sub = ew >> 2;           // 0..3
-    const int r = q * 32 + lane;       // tile row owned by this thread
     constexpr int kOutCols = D / 4;
     int it = 0;
     bool ok = true;
@@ -504,9 +503,17 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
       }
       if (!ok) break;
 
-      // Output: acc2 + b2 -> bf16 rows of Y.
+      // Output: acc2 + b2 -> bf16 rows of Y.  A thread holds kOutCols
+      // columns of its row, kU units of 16 columns (32 bytes).  A transpose
+      // of units inside each group of kU lanes (log2(kU) butterfly steps of
+      // shuffles) leaves lane i, in slot k, unit i % kU of row
+      // i - i % kU + k, so that kU lanes store one contiguous row segment
+      // together instead of every lane writing to a different row.
+      constexpr int kU = kOutCols / 16;  // 4 at D=256, 2 at D=128
       const float4* bo4 = reinterpret_cast<const float4*>(b2 + (int64_t)gw * D + sub * kOutCols);
-      if (!mbar_wait(a2_full, (uint32_t)(it & 1), status, 0x20e, abort_flag)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(a2_full, (uint32_t)(it & 1), status, 0x20e,
+                                             abort_flag)))
+        break;
       tc_fence_after();
       uint32_t o[kOutCols];
       const uint32_t taddr2 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)sub * kOutCols;
@@ -520,18 +527,41 @@ __global__ void __launch_bounds__(GATHER ? kThreads + 32 : kThreads, 1)
       tmem_ld_wait();
       tc_fence_before();
       warp_arrive(a2_empty, lane);
-      if (r < tc.rows) {
-        uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)tc.row0 + r) * D + sub * kOutCols);
+      uint32_t u[kU][8];  // unit j, word w: columns 16j + 2w, 16j + 2w + 1
 #pragma unroll
-        for (int j = 0; j < kOutCols / 8; ++j) {
-          const float4 c0 = __ldg(bo4 + 2 * j), c1 = __ldg(bo4 + 2 * j + 1);
-          uint4 pk;
-          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + c0.x, __uint_as_float(o[8 * j + 1]) + c0.y);
-          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + c0.z, __uint_as_float(o[8 * j + 3]) + c0.w);
-          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + c1.x, __uint_as_float(o[8 * j + 5]) + c1.y);
-          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + c1.z, __uint_as_float(o[8 * j + 7]) + c1.w);
-          dst[j] = pk;
+      for (int j = 0; j < kU; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 cb = __ldg(bo4 + 4 * j + i);
+          u[j][2 * i] = pack_bf16x2(__uint_as_float(o[16 * j + 4 * i]) + cb.x,
+                                    __uint_as_float(o[16 * j + 4 * i + 1]) + cb.y);
+          u[j][2 * i + 1] = pack_bf16x2(__uint_as_float(o[16 * j + 4 * i + 2]) + cb.z,
+                                        __uint_as_float(o[16 * j + 4 * i + 3]) + cb.w);
         }
+#pragma unroll
+      for (int m = 1; m < kU; m <<= 1) {
+        // Lanes i and i ^ m swap the units whose bit m differs from theirs.
+        const bool hi = (lane & m) != 0;
+#pragma unroll
+        for (int j = 0; j < kU; ++j) {
+          if (j & m) continue;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t got = __shfl_xor_sync(0xffffffffu, hi ? u[j][w] : u[j ^ m][w], m);
+            if (hi)
+              u[j][w] = got;
+            else
+              u[j ^ m][w] = got;
+          }
+        }
+      }
+      const bool y32 = (reinterpret_cast<uintptr_t>(Y) & 31) == 0;
+#pragma unroll
+      for (int k = 0; k < kU; ++k) {
+        const int rr = q * 32 + (lane & ~(kU - 1)) + k;
+        if (rr < tc.rows)
+          st_global_32B(Y + ((int64_t)tc.row0 + rr) * D + sub * kOutCols + 16 * (lane & (kU - 1)),
+                        u[k], y32);
       }
     }
   }
