@@ -4,9 +4,7 @@
 //
 // issued as one tcgen05.mma.cta_group::2 stream for both SMs of a
 // thread-block cluster of two.  Every MMA is M = 256 (128 rows per SM) x
-// N = 256 x K = 16, so each instruction gives each SM 128 cycles of tensor
-// work - more than the ~100-cycle issue interval of a pair MMA, and enough to
-// hide the barrier tests of the issuing thread.
+// N = 256 x K = 16: each instruction gives each SM 128 cycles of tensor work.
 //
 // Per tile, d_ff is processed in 256-wide chunks c:
 //   GEMM1(c): acc1 (TMEM, 256 fp32 columns) = X[256, D] @ W1[e][c*256:+256, :]^T
@@ -22,21 +20,27 @@
 // acc1 / acc2 in its TMEM) and HALF of every weight K-slab ([128 x 64]: the
 // W1 rows [c*256 + 128r, +128) or the W2 output rows [128r, +128) of the
 // chunk, r = its rank), so each SM streams half the weight bytes per FLOP of
-// a one-SM tile.  Weights stream through a ring of kRing K-slabs in the
-// order the MMAs consume them (GEMM1(c) slabs, then GEMM2(c-1) slabs).  The
+// a one-SM tile.  W1 and W2 slabs stream through two rings of their own
+// (4 and 2 slabs), each filled by a producer warp: GEMM2's slabs wait in
+// their ring until the epilogue has written the matching H slab, and with
+// one ring for both they held the slots GEMM1(c+1)'s slabs needed.  The
 // even CTA (leader) issues every MMA; the barriers it waits on live in its
 // shared memory - the peer's TMA loads complete on them (.cta_group::2) and
 // the peer's epilogue warps arrive on them through shared::cluster
 // addresses; MMA completions that both CTAs wait for are committed twice,
 // once to each CTA's copy of the barrier.
 //
-// Roles per CTA (576 threads): warp 0 TMA producer, warp 1 TMEM allocation
-// for the pair and (leader) MMA issuer, warps 2-17 epilogue.  Epilogue warp
-// (lane quadrant q, group s) owns rows 32q..32q+31 and, of every 64-wide
-// K slab, columns [16s, 16s + 16).
+// Roles per CTA (608 threads): warp 0 TMA producer of X and W1, warp 1 TMEM
+// allocation for the pair and (leader) MMA issuer, warp 2 TMA producer of
+// W2, warps 3-18 epilogue.  Epilogue warp (lane quadrant q, group s) owns
+// rows 32q..32q+31 and, of every 64-wide K slab, columns [16s, 16s + 16).
+// Biases are read through the read-only cache, one slab ahead.  The output
+// rows go out transposed inside groups of four lanes, so that each 32-byte
+// store of a warp writes four whole 128-byte row segments.
 // TMEM per CTA: acc2 columns [0, 256), acc1 [256, 512).
-// Shared memory per CTA: X 64 KB + ring 5 x 16 KB + H 64 KB + biases 5 KB +
-// scheduler 2 KB.  d_model 256; d_ff a multiple of 256 up to 1024.
+// Shared memory per CTA: barriers and scheduler first, then (1024-aligned)
+// X 64 KB + H 64 KB + W1 ring 64 KB + W2 ring 32 KB.  d_model 256; d_ff a
+// multiple of 256 up to 1024.
 //
 // Every wait is bounded (common.cuh); a CTA that gives up sets its abort
 // flag, its roles unwind, the peer's waits run out in turn, and both CTAs
@@ -55,29 +59,27 @@ constexpr int kPFC = 256;              // d_ff chunk
 constexpr int kPBK = 64;               // bf16 per 128-byte swizzled row
 constexpr int kPSlabs = kPD / kPBK;    // 4 K slabs of X, of a W1 chunk, of a W2 chunk, of H
 constexpr int kPEpiWarps = 16;
-constexpr int kPThreads = 64 + kPEpiWarps * 32;
+constexpr int kPEpi0 = 3;              // first epilogue warp
+constexpr int kPThreads = 32 * kPEpi0 + kPEpiWarps * 32;
 constexpr int kPMaxF = 1024;
-constexpr int kRing = 5;               // weight K slabs in flight
+constexpr int kW1Ring = 4;             // W1 K slabs in flight
+constexpr int kW2Ring = 2;             // W2 K slabs in flight
 constexpr uint32_t kPAcc1Col = 256;
-using PSched = GroupSchedT<256>;
+using PSched = GroupSchedT<128>;
 
 constexpr size_t kPSlab = (size_t)kPBM * kPBK * 2;            // 16 KB: [128 x 64] bf16
 constexpr size_t kPXBytes = kPSlabs * kPSlab;                  // 64 KB
 constexpr size_t kPHBytes = kPSlabs * kPSlab;                  // 64 KB
-constexpr size_t kPRingBytes = kRing * kPSlab;                 // 80 KB
-constexpr size_t kPBias = (size_t)(kPMaxF + kPD) * 4;
-constexpr size_t kPSmem = 1024 + kPXBytes + kPHBytes + kPRingBytes + kPBias +
-                          PSched::smem_bytes() + 512;
+constexpr size_t kPW1Bytes = kW1Ring * kPSlab;                 // 64 KB
+constexpr size_t kPW2Bytes = kW2Ring * kPSlab;                 // 32 KB
+constexpr size_t kPBarBytes = 512;
+constexpr size_t kPSmall = kPBarBytes + PSched::smem_bytes();  // ahead of the aligned part
+constexpr size_t kPSmem = kPSmall + 1023 + kPXBytes + kPHBytes + kPW1Bytes + kPW2Bytes;
 static_assert(kPSmem <= 232448, "shared memory per CTA");
 
 CTI_DEVICE void pair_warp_arrive_local(uint64_t* bar, int lane) {
   __syncwarp();
   if (lane == 0) mbar_arrive(bar);
-}
-
-CTI_DEVICE void pair_warp_arrive_remote(uint32_t cluster_bar, int lane) {
-  __syncwarp();
-  if (lane == 0) mbar_arrive_cluster(cluster_bar);
 }
 
 // Commits the completion of every pair MMA issued so far to the barrier at
@@ -92,6 +94,38 @@ CTI_DEVICE void st_swizzled16(uint8_t* slab, int r, int j, uint4 v) {
   *reinterpret_cast<uint4*>(slab + r * 128 + ((j ^ (r & 7)) << 4)) = v;
 }
 
+// This thread's 16 b1 values of one K slab.
+CTI_DEVICE void load_bias16(float4 (&b)[4], const float* p) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b[i] = __ldg(reinterpret_cast<const float4*>(p) + i);
+}
+
+// One weight K slab of this CTA's half into ring slot n % slots, once the
+// MMAs reading the slot's previous contents have completed.  The leader's
+// full barrier counts the bytes of both CTAs.
+CTI_DEVICE bool load_pair_slab(uint8_t* ring, uint64_t* full, uint64_t* empty,
+                               const uint32_t* full_c, int slots, int& n, const CUtensorMap* map,
+                               int k0, int row0, bool leader, int32_t* status, int where,
+                               volatile int* abort_flag) {
+  const int slot = n % slots;
+  if (!mbar_wait_cluster(&empty[slot], (uint32_t)((n / slots) & 1) ^ 1u, status, where,
+                         abort_flag))
+    return false;
+  if (leader) mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * kPSlab));
+  tma_load_2d_pair(ring + slot * kPSlab, map, full_c[slot], k0, row0);
+  ++n;
+  return true;
+}
+
+// The leader waits for the last armed phase of each slot of a ring (both
+// CTAs' bytes), so that no load of either CTA is still in flight.
+CTI_DEVICE void drain_ring(uint64_t* full, int slots, int n, int32_t* status, int where) {
+  for (int i = 1; i <= slots; ++i)
+    if (n - i >= 0)
+      mbar_wait_cluster(&full[(n - i) % slots], (uint32_t)(((n - i) / slots) & 1), status, where,
+                        nullptr);
+}
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     fused_ffn_pair_kernel(const __grid_constant__ CUtensorMap tmX,
                           const __grid_constant__ CUtensorMap tmW1,
@@ -100,33 +134,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                           int64_t rows_total, int F, const float* __restrict__ b1,
                           const float* __restrict__ b2, int act,
                           __nv_bfloat16* __restrict__ Y, int32_t* status) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+  uint8_t* sched_mem = smem_raw + kPBarBytes;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw + kPSmall) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sx = smem;
   uint8_t* sh = sx + kPXBytes;          // H(c): 4 K slabs [128 x 64]
-  uint8_t* ring = sh + kPHBytes;        // weight K slabs
-  float* b1s = reinterpret_cast<float*>(ring + kPRingBytes);
-  float* b2s = b1s + kPMaxF;
-  uint8_t* sched_mem = reinterpret_cast<uint8_t*>(b2s + kPD);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sched_mem + PSched::smem_bytes());
+  uint8_t* ring1 = sh + kPHBytes;       // W1 K slabs
+  uint8_t* ring2 = ring1 + kPW1Bytes;   // W2 K slabs
   // Waited on by the leader's MMA thread (arrivals and bytes from both CTAs):
-  uint64_t* full = bars;                 // [kRing] weight slab of both CTAs landed
-  uint64_t* x_full = full + kRing;       // X rows of both CTAs landed
-  uint64_t* acc1_free = x_full + 1;      // both epilogues have drained acc1
-  uint64_t* h_full = acc1_free + 1;      // [4] H slab written by both epilogues
-  uint64_t* a2_empty = h_full + kPSlabs; // both epilogues have read acc2
+  uint64_t* full1 = bars;                 // [kW1Ring] W1 slab of both CTAs landed
+  uint64_t* full2 = full1 + kW1Ring;      // [kW2Ring] W2 slab of both CTAs landed
+  uint64_t* x_full = full2 + kW2Ring;     // X rows of both CTAs landed
+  uint64_t* acc1_free = x_full + 1;       // both epilogues have drained acc1
+  uint64_t* h_full = acc1_free + 1;       // [4] H slab written by both epilogues
+  uint64_t* a2_empty = h_full + kPSlabs;  // both epilogues have read acc2
   uint64_t* drain = a2_empty + 1;
+  // The peer's epilogue arrives on these local copies; its forwarding thread
+  // passes each completed phase on to the leader with one cluster arrival.
+  uint64_t* acc1_fwd = drain + 1;
+  uint64_t* h_fwd = acc1_fwd + 1;         // [4]
+  uint64_t* a2_fwd = h_fwd + kPSlabs;
   // Waited on in each CTA (committed by the leader to both copies):
-  uint64_t* empty = drain + 1;           // [kRing] weight slot may be refilled
-  uint64_t* x_empty = empty + kRing;
-  uint64_t* a1_full = x_empty + 1;       // GEMM1(c) done
-  uint64_t* h_empty = a1_full + 1;       // [4] GEMM2 has read H slab kb
-  uint64_t* a2_full = h_empty + kPSlabs; // GEMM2 of the tile's last chunk done
-  // Local to the epilogue of each CTA:
-  uint64_t* bfree = a2_full + 1;
-  uint64_t* bready = bfree + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bready + 1);
+  uint64_t* empty1 = a2_fwd + 1;          // [kW1Ring] W1 slot may be refilled
+  uint64_t* empty2 = empty1 + kW1Ring;    // [kW2Ring] W2 slot may be refilled
+  uint64_t* x_empty = empty2 + kW2Ring;
+  uint64_t* a1_full = x_empty + 1;        // GEMM1(c) done
+  uint64_t* h_empty = a1_full + 1;        // [4] GEMM2 has read H slab kb
+  uint64_t* a2_full = h_empty + kPSlabs;  // GEMM2 of the tile's last chunk done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a2_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -138,23 +175,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRing; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kW1Ring; ++s) {
+      mbar_init(&full1[s], 1);
+      mbar_init(&empty1[s], 1);
+    }
+    for (int s = 0; s < kW2Ring; ++s) {
+      mbar_init(&full2[s], 1);
+      mbar_init(&empty2[s], 1);
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 1);
-    mbar_init(acc1_free, 2 * kPEpiWarps);
+    // Leader: its own epilogue warps plus the peer's forwarding thread.
+    mbar_init(acc1_free, kPEpiWarps + 1);
+    mbar_init(acc1_fwd, kPEpiWarps);
     for (int i = 0; i < kPSlabs; ++i) {
-      mbar_init(&h_full[i], 2 * kPEpiWarps);
+      mbar_init(&h_full[i], kPEpiWarps + 1);
+      mbar_init(&h_fwd[i], kPEpiWarps);
       mbar_init(&h_empty[i], 1);
     }
-    mbar_init(a2_empty, 2 * kPEpiWarps);
+    mbar_init(a2_empty, kPEpiWarps + 1);
+    mbar_init(a2_fwd, kPEpiWarps);
     mbar_init(drain, 1);
     mbar_init(a1_full, 1);
     mbar_init(a2_full, 1);
-    mbar_init(bfree, kPEpiWarps);
-    mbar_init(bready, kPEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -180,25 +223,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int total = sched.total_tiles();
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------ X / W1 producer
     if (lane == 0) {
-      uint32_t full_c[kRing];
-      for (int s = 0; s < kRing; ++s) full_c[s] = mapa_shared(&full[s], 0);
+      uint32_t full_c[kW1Ring];
+      for (int s = 0; s < kW1Ring; ++s) full_c[s] = mapa_shared(&full1[s], 0);
       const uint32_t x_full_c = mapa_shared(x_full, 0);
-      int n = 0, x_issued = 0;  // weight slabs issued, X tiles issued
+      int n = 0, x_issued = 0;  // W1 slabs issued, X tiles issued
       int it = 0;
       bool ok = true;
-      // One weight K slab (this CTA's [128 x 64] half) into the next ring slot.
-      auto load_slab = [&](const CUtensorMap* map, int k0, int row0) -> bool {
-        const int slot = n % kRing;
-        if (!mbar_wait_cluster(&empty[slot], (uint32_t)((n / kRing) & 1) ^ 1u, status, 0x401,
-                               abort_flag))
-          return false;
-        if (leader) mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * kPSlab));
-        tma_load_2d_pair(ring + slot * kPSlab, map, full_c[slot], k0, row0);
-        ++n;
-        return true;
-      };
       for (int t = pair; t < total && ok; t += npairs, ++it) {
         const TileCoord tc = sched.decode(t);
         const int gw = tc.g % Gw;
@@ -213,51 +245,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           for (int kb = 0; kb < kPSlabs; ++kb)
             tma_prefetch_l2_2d(&tmX, kb * kPBK, nx.row0 + (int)rank * kPBM);
         }
-        // The MMAs' order: GEMM1(c) slabs, then GEMM2(c-1) slabs.
-        for (int c = 0; c <= nch && ok; ++c) {
-          if (c < nch)
-            for (int kb = 0; kb < kPSlabs && ok; ++kb)
-              ok = load_slab(&tmW1, kb * kPBK, gw * F + c * kPFC + (int)rank * kPBM);
-          if (c >= 1)
-            for (int kb = 0; kb < kPSlabs && ok; ++kb)
-              ok = load_slab(&tmW2, (c - 1) * kPFC + kb * kPBK, gw * kPD + (int)rank * kPBM);
-        }
+        for (int c = 0; c < nch && ok; ++c)
+          for (int kb = 0; kb < kPSlabs && ok; ++kb)
+            ok = load_pair_slab(ring1, full1, empty1, full_c, kW1Ring, n, &tmW1, kb * kPBK,
+                                gw * F + c * kPFC + (int)rank * kPBM, leader, status, 0x401,
+                                abort_flag);
       }
-      // The leader's full barriers count both CTAs' bytes: once their last
-      // armed phases complete, no load of either CTA is in flight.
       if (leader) {
-        for (int i = 1; i <= kRing; ++i)
-          if (n - i >= 0)
-            mbar_wait_cluster(&full[(n - i) % kRing], (uint32_t)(((n - i) / kRing) & 1), status,
-                              0x403, nullptr);
+        drain_ring(full1, kW1Ring, n, status, 0x403);
         if (x_issued > 0)
           mbar_wait_cluster(x_full, (uint32_t)((x_issued - 1) & 1), status, 0x403, nullptr);
       }
+    }
+  } else if (warp == 2) {
+    // ----------------------------------------------------------- W2 producer
+    if (lane == 0) {
+      uint32_t full_c[kW2Ring];
+      for (int s = 0; s < kW2Ring; ++s) full_c[s] = mapa_shared(&full2[s], 0);
+      int n = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += npairs) {
+        const int gw = sched.decode(t).g % Gw;
+        for (int c = 0; c < nch && ok; ++c)
+          for (int kb = 0; kb < kPSlabs && ok; ++kb)
+            ok = load_pair_slab(ring2, full2, empty2, full_c, kW2Ring, n, &tmW2,
+                                c * kPFC + kb * kPBK, gw * kPD + (int)rank * kPBM, leader, status,
+                                0x411, abort_flag);
+      }
+      if (leader) drain_ring(full2, kW2Ring, n, status, 0x412);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(2 * kPBM, 256);  // M 256, N 256 (both GEMMs)
-      int n = 0;        // weight slabs consumed
-      int gc = 0;       // GEMM1s issued (global chunk counter)
+      int n1 = 0, n2 = 0;  // W1 / W2 slabs consumed
+      int gc = 0;          // GEMM1s issued (global chunk counter)
       int it = 0;
       bool any = false, ok = true;
       const uint32_t x_addr = smem_u32(sx);
       const uint32_t h_addr = smem_u32(sh);
-      const uint32_t ring_addr = smem_u32(ring);
+      const uint32_t ring1_addr = smem_u32(ring1);
+      const uint32_t ring2_addr = smem_u32(ring2);
       const uint32_t acc1 = tmem_base + kPAcc1Col;
-      auto wait_slab = [&](uint32_t& b_addr) -> bool {
-        const int slot = n % kRing;
-        if (!mbar_wait_cluster(&full[slot], (uint32_t)((n / kRing) & 1), status, 0x405,
-                               abort_flag))
-          return false;
-        b_addr = ring_addr + (uint32_t)(slot * kPSlab);
-        return true;
-      };
-      auto release_slab = [&]() {
-        commit_both(&empty[n % kRing]);
-        ++n;
-      };
       for (int t = pair; t < total && ok; t += npairs, ++it) {
         if (!mbar_wait_cluster(x_full, (uint32_t)(it & 1), status, 0x404, abort_flag)) break;
         tc_fence_after();
@@ -268,19 +297,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               ok = false;
               break;
             }
-            tc_fence_after();
-            for (int kb = 0; kb < kPSlabs && ok; ++kb) {
-              uint32_t b0;
-              if (!wait_slab(b0)) {
+            for (int kb = 0; kb < kPSlabs; ++kb) {
+              const int slot = n1 % kW1Ring;
+              if (!mbar_wait_cluster(&full1[slot], (uint32_t)((n1 / kW1Ring) & 1), status, 0x405,
+                                     abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
+              const uint32_t b0 = ring1_addr + (uint32_t)(slot * kPSlab);
 #pragma unroll
               for (int kk = 0; kk < kPBK / 16; ++kk)
                 umma_bf16_pair(acc1, smem_desc_sw128(x_addr + kb * kPSlab + kk * 32),
                                smem_desc_sw128(b0 + kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
-              release_slab();
+              commit_both(&empty1[slot]);
+              ++n1;
             }
             if (!ok) break;
             commit_both(a1_full);
@@ -296,20 +327,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               ok = false;
               break;
             }
-            for (int kb = 0; kb < kPSlabs && ok; ++kb) {
-              uint32_t b0;
-              if (!wait_slab(b0) ||
+            for (int kb = 0; kb < kPSlabs; ++kb) {
+              const int slot = n2 % kW2Ring;
+              if (!mbar_wait_cluster(&full2[slot], (uint32_t)((n2 / kW2Ring) & 1), status, 0x413,
+                                     abort_flag) ||
                   !mbar_wait_cluster(&h_full[kb], hph, status, 0x408, abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
+              const uint32_t b0 = ring2_addr + (uint32_t)(slot * kPSlab);
 #pragma unroll
               for (int kk = 0; kk < kPBK / 16; ++kk)
                 umma_bf16_pair(tmem_base, smem_desc_sw128(h_addr + kb * kPSlab + kk * 32),
                                smem_desc_sw128(b0 + kk * 32), idesc,
                                (cc | kb | kk) != 0 ? 1u : 0u);
-              release_slab();
+              commit_both(&empty2[slot]);
+              ++n2;
               commit_both(&h_empty[kb]);
             }
             if (!ok) break;
@@ -321,42 +355,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         umma_commit_pair(mapa_shared(drain, 0));
         mbar_wait_cluster(drain, 0, status, 0x409, nullptr);
       }
+    } else if (!leader && lane == 0) {
+      // ---------------------------------------------- peer: forwarding thread
+      // A cluster-scope release arrival costs its thread ~1.7 K cycles; one
+      // thread pays it per event instead of each epilogue warp.
+      const uint32_t acc1_free_c = mapa_shared(acc1_free, 0);
+      const uint32_t a2_empty_c = mapa_shared(a2_empty, 0);
+      uint32_t h_full_c[kPSlabs];
+      for (int i = 0; i < kPSlabs; ++i) h_full_c[i] = mapa_shared(&h_full[i], 0);
+      int gc = 0;
+      bool ok = true;
+      for (int t = pair, it = 0; t < total && ok; t += npairs, ++it) {
+        for (int c = 0; c < nch && ok; ++c, ++gc) {
+          if (!mbar_wait(acc1_fwd, (uint32_t)(gc & 1), status, 0x414, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(acc1_free_c);
+          for (int kb = 0; kb < kPSlabs; ++kb) {
+            if (!mbar_wait(&h_fwd[kb], (uint32_t)(gc & 1), status, 0x415, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_cluster(h_full_c[kb]);
+          }
+        }
+        if (!ok || !mbar_wait(a2_fwd, (uint32_t)(it & 1), status, 0x416, abort_flag)) break;
+        mbar_arrive_cluster(a2_empty_c);
+      }
     }
-  } else {
+  } else if (warp >= kPEpi0) {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;
+    const int ew = warp - kPEpi0;
     const int q = warp & 3;            // TMEM lane quadrant
     const int sub = ew >> 2;           // columns [16 sub, +16) of every K slab
     const int r = q * 32 + lane;       // row of this CTA's 128
-    const int etid = ew * 32 + lane;
     constexpr int kOutCols = kPD / 4;
-    uint32_t h_full_c[kPSlabs];
-    for (int i = 0; i < kPSlabs; ++i) h_full_c[i] = mapa_shared(&h_full[i], 0);
-    const uint32_t acc1_free_c = mapa_shared(acc1_free, 0);
-    const uint32_t a2_empty_c = mapa_shared(a2_empty, 0);
+    // The leader's warps arrive on its barriers directly; the peer's on local
+    // copies that its forwarding thread passes on.
+    uint64_t* acc1_sig = leader ? acc1_free : acc1_fwd;
+    uint64_t* h_sig = leader ? h_full : h_fwd;
+    uint64_t* a2_sig = leader ? a2_empty : a2_fwd;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    const bool y32 = (reinterpret_cast<uintptr_t>(Y) & 31) == 0;
     int it = 0, gc = 0;
-    int staged_gw = -1;
-    uint32_t n_staged = 0;
     bool ok = true;
     for (int t = pair; t < total && ok; t += npairs, ++it) {
       const TileCoord tc = sched.decode(t);
       const int gw = tc.g % Gw;
       const int my_row0 = tc.row0 + (int)rank * kPBM;
       const int my_rows = tc.rows - (int)rank * kPBM;  // may be <= 0 in the last tile
-      if (gw != staged_gw) {
-        if (n_staged > 0) {
-          pair_warp_arrive_local(bfree, lane);
-          if (!mbar_wait(bfree, (n_staged - 1) & 1u, status, 0x40f, abort_flag)) break;
-        }
-        for (int i = etid; i < F; i += kPEpiWarps * 32) b1s[i] = b1[(int64_t)gw * F + i];
-        for (int i = etid; i < kPD; i += kPEpiWarps * 32) b2s[i] = b2[(int64_t)gw * kPD + i];
-        pair_warp_arrive_local(bready, lane);
-        if (!mbar_wait(bready, n_staged & 1u, status, 0x410, abort_flag)) break;
-        ++n_staged;
-        staged_gw = gw;
-      }
+      const float* b1e = b1 + (int64_t)gw * F + sub * 16;
       for (int c = 0; c < nch; ++c, ++gc) {
+        float4 bias[4];
+        load_bias16(bias, b1e + c * kPFC);  // slab 0's, ahead of the accumulator wait
         if (!mbar_wait_cluster(a1_full, (uint32_t)(gc & 1), status, 0x40c, abort_flag)) {
           ok = false;
           break;
@@ -369,20 +421,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           tmem_ld_32x32b_x16(lane_base + kPAcc1Col + (uint32_t)(kb * kPBK + sub * 16), v[kb]);
         tmem_ld_wait();
         tc_fence_before();
-        pair_warp_arrive_remote(acc1_free_c, lane);
+        pair_warp_arrive_local(acc1_sig, lane);
 #pragma unroll
         for (int kb = 0; kb < kPSlabs; ++kb) {
-          const float4* bc =
-              reinterpret_cast<const float4*>(b1s + c * kPFC + kb * kPBK + sub * 16);
           float a[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 bb = bc[i];
-            a[4 * i + 0] = __uint_as_float(v[kb][4 * i + 0]) + bb.x;
-            a[4 * i + 1] = __uint_as_float(v[kb][4 * i + 1]) + bb.y;
-            a[4 * i + 2] = __uint_as_float(v[kb][4 * i + 2]) + bb.z;
-            a[4 * i + 3] = __uint_as_float(v[kb][4 * i + 3]) + bb.w;
+          for (int i = 0; i < 4; ++i) {  // + b1, two values per packed add
+            const float4 bb = bias[i];
+            f2_unpack(f2_add(f2_pack(__uint_as_float(v[kb][4 * i + 0]),
+                                     __uint_as_float(v[kb][4 * i + 1])),
+                             f2_pack(bb.x, bb.y)),
+                      a[4 * i + 0], a[4 * i + 1]);
+            f2_unpack(f2_add(f2_pack(__uint_as_float(v[kb][4 * i + 2]),
+                                     __uint_as_float(v[kb][4 * i + 3])),
+                             f2_pack(bb.z, bb.w)),
+                      a[4 * i + 2], a[4 * i + 3]);
           }
+          if (kb + 1 < kPSlabs) load_bias16(bias, b1e + c * kPFC + (kb + 1) * kPBK);
           act_n<16>(act, a);
           uint4 w0, w1;
           w0.x = pack_bf16x2(a[0], a[1]);
@@ -404,14 +459,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           st_swizzled16(slab, r, 2 * sub, w0);
           st_swizzled16(slab, r, 2 * sub + 1, w1);
           fence_proxy_async_smem();  // visible to the tensor core's operand reads
-          pair_warp_arrive_remote(h_full_c[kb], lane);
+          pair_warp_arrive_local(&h_sig[kb], lane);
         }
         if (!ok) break;
       }
       if (!ok) break;
 
       // Output: acc2 + b2 -> bf16 rows of Y (this CTA's rows of the tile).
-      if (!mbar_wait_cluster(a2_full, (uint32_t)(it & 1), status, 0x40e, abort_flag)) break;
+      // A thread holds kOutCols columns of its row, four units of 16 columns
+      // (32 bytes); a transpose of units inside each group of four lanes
+      // (two butterfly steps of shuffles) leaves lane i, in slot k, unit
+      // i % 4 of row i - i % 4 + k, so four lanes store one row segment.
+      const float4* bo4 = reinterpret_cast<const float4*>(b2 + (int64_t)gw * kPD + sub * kOutCols);
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(a2_full, (uint32_t)(it & 1), status, 0x40e,
+                                                     abort_flag)))
+        break;
       tc_fence_after();
       uint32_t o[kOutCols];
       const uint32_t taddr2 = lane_base + (uint32_t)sub * kOutCols;
@@ -424,23 +486,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       }
       tmem_ld_wait();
       tc_fence_before();
-      pair_warp_arrive_remote(a2_empty_c, lane);
-      if (r < my_rows) {
-        const float* bo = b2s + sub * kOutCols;
-        uint4* dst = reinterpret_cast<uint4*>(Y + ((int64_t)my_row0 + r) * kPD + sub * kOutCols);
+      pair_warp_arrive_local(a2_sig, lane);
+      constexpr int kU = kOutCols / 16;
+      uint32_t u[kU][8];  // unit j, word w: columns 16j + 2w, 16j + 2w + 1
 #pragma unroll
-        for (int j = 0; j < kOutCols / 8; ++j) {
-          uint4 pk;
-          pk.x = pack_bf16x2(__uint_as_float(o[8 * j]) + bo[8 * j],
-                             __uint_as_float(o[8 * j + 1]) + bo[8 * j + 1]);
-          pk.y = pack_bf16x2(__uint_as_float(o[8 * j + 2]) + bo[8 * j + 2],
-                             __uint_as_float(o[8 * j + 3]) + bo[8 * j + 3]);
-          pk.z = pack_bf16x2(__uint_as_float(o[8 * j + 4]) + bo[8 * j + 4],
-                             __uint_as_float(o[8 * j + 5]) + bo[8 * j + 5]);
-          pk.w = pack_bf16x2(__uint_as_float(o[8 * j + 6]) + bo[8 * j + 6],
-                             __uint_as_float(o[8 * j + 7]) + bo[8 * j + 7]);
-          dst[j] = pk;
+      for (int j = 0; j < kU; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 cb = __ldg(bo4 + 4 * j + i);
+          u[j][2 * i] = pack_bf16x2(__uint_as_float(o[16 * j + 4 * i]) + cb.x,
+                                    __uint_as_float(o[16 * j + 4 * i + 1]) + cb.y);
+          u[j][2 * i + 1] = pack_bf16x2(__uint_as_float(o[16 * j + 4 * i + 2]) + cb.z,
+                                        __uint_as_float(o[16 * j + 4 * i + 3]) + cb.w);
         }
+#pragma unroll
+      for (int m = 1; m < kU; m <<= 1) {
+        // Lanes i and i ^ m swap the units whose bit m differs from theirs.
+        const bool hi = (lane & m) != 0;
+#pragma unroll
+        for (int j = 0; j < kU; ++j) {
+          if (j & m) continue;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t got = __shfl_xor_sync(0xffffffffu, hi ? u[j][w] : u[j ^ m][w], m);
+            if (hi)
+              u[j][w] = got;
+            else
+              u[j ^ m][w] = got;
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kU; ++k) {
+        const int rr = q * 32 + (lane & ~(kU - 1)) + k;
+        if (rr < my_rows)
+          st_global_32B(Y + ((int64_t)my_row0 + rr) * kPD + sub * kOutCols + 16 * (lane & (kU - 1)),
+                        u[k], y32);
       }
     }
   }
