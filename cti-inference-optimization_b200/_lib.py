@@ -74,7 +74,7 @@ SIGNATURES = {
     "cti_moe_layer_forward_host": (
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _I64, _P, _SZ, _P,
-         _P, _P, _P],
+         _P, _P, _P, _P],
     ),
     "cti_embbag_sum": (
         _I,

@@ -156,10 +156,14 @@ extern "C" int cti_moe_layer_forward(const void* x_bf16, const float* wg, const 
 }
 
 // The whole layer between pinned host buffers, pipelined over chunks of
-// tokens on three streams:
+// tokens on three streams (four with a second compute stream):
 //   copy_in:  H2D of x chunk i            -> record ev_in
 //   stream:   wait ev_in; layer on chunk i -> record ev_out
 //   copy_out: wait ev_out; D2H of out chunk i
+// With compute_stream2, odd chunks' layers run there, on the second half of
+// the workspace, so that two chunks' layers overlap: a layer of a few
+// thousand tokens fills only part of the GPU and costs ~50 us whatever its
+// size, which otherwise sets the pace of small chunks.
 // cudaStreamWaitEvent binds to the event's latest record at the time of
 // the call, so three events serve every chunk.  Every token's output
 // depends only on its own row (router, expert rows and combine are
@@ -169,14 +173,18 @@ extern "C" int cti_moe_layer_forward_host(
     const float* bg, const void* W1_bf16, const float* b1, const void* W2_bf16, const float* b2,
     int64_t T, int D, int E, int F, int act, int renorm, int64_t chunk_tokens, void* workspace,
     size_t workspace_bytes, int32_t* status, void* stream, void* copy_stream_in,
-    void* copy_stream_out) {
+    void* copy_stream_out, void* compute_stream2) {
   if (T < 0 || D <= 0 || E < 2 || F <= 0 || chunk_tokens <= 0) return CTI_ERR_INVALID_ARG;
   if (T == 0) return CTI_OK;
   if (!x_host || !out_host || !x_dev || !out_dev) return CTI_ERR_INVALID_ARG;
   const int64_t chunk = chunk_tokens < T ? chunk_tokens : T;
-  if (!workspace || workspace_bytes < cti_moe_layer_workspace_bytes(chunk, D, E, F))
+  const size_t ws_need = cti_moe_layer_workspace_bytes(chunk, D, E, F);
+  const size_t ws_half = align_up(ws_need);  // offset of the second half
+  const bool two = compute_stream2 != nullptr;
+  if (!workspace || workspace_bytes < (two ? ws_half + ws_need : ws_need))
     return CTI_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStream_t s2 = two ? static_cast<cudaStream_t>(compute_stream2) : s;
   cudaStream_t s_in = static_cast<cudaStream_t>(copy_stream_in);
   cudaStream_t s_out = static_cast<cudaStream_t>(copy_stream_out);
   const int64_t nchunks = (T + chunk - 1) / chunk;
@@ -196,8 +204,9 @@ extern "C" int cti_moe_layer_forward_host(
   };
   const size_t row_bytes = (size_t)D * 2;
   // The copies start after everything already enqueued on `stream`.
-  if (cuda_ok(cudaEventRecord(ev[0], s)) && cuda_ok(cudaStreamWaitEvent(s_in, ev[0], 0)))
-    cuda_ok(cudaStreamWaitEvent(s_out, ev[0], 0));
+  if (cuda_ok(cudaEventRecord(ev[0], s)) && cuda_ok(cudaStreamWaitEvent(s_in, ev[0], 0)) &&
+      cuda_ok(cudaStreamWaitEvent(s_out, ev[0], 0)) && two)
+    cuda_ok(cudaStreamWaitEvent(s2, ev[0], 0));
   // Every chunk's copy in first, so that the copy stream runs back to back
   // whatever the host's launch rate for the layers below.
   int64_t copied = 0;
@@ -218,11 +227,17 @@ extern "C" int cti_moe_layer_forward_host(
     const size_t off = (size_t)t0 * row_bytes, bytes = (size_t)n * row_bytes;
     uint8_t* xd = static_cast<uint8_t*>(x_dev) + off;
     uint8_t* od = static_cast<uint8_t*>(out_dev) + off;
-    if (!cuda_ok(cudaStreamWaitEvent(s, ev[2 + i], 0))) break;
+    // Layers alternate between the two compute streams and workspace halves;
+    // a stream's next layer reuses its half only after its previous one.
+    const bool odd = two && (i & 1);
+    cudaStream_t sl = odd ? s2 : s;
+    void* wsl = odd ? static_cast<void*>(static_cast<uint8_t*>(workspace) + ws_half) : workspace;
+    const size_t wsl_bytes = odd ? workspace_bytes - ws_half : (two ? ws_half : workspace_bytes);
+    if (!cuda_ok(cudaStreamWaitEvent(sl, ev[2 + i], 0))) break;
     rc = cti_moe_layer_forward(xd, wg, bg, W1_bf16, b1, W2_bf16, b2, n, D, E, F, act, renorm, od,
-                               workspace, workspace_bytes, status, stream);
+                               wsl, wsl_bytes, status, sl);
     if (rc != CTI_OK) break;
-    if (!cuda_ok(cudaEventRecord(ev[1], s)) || !cuda_ok(cudaStreamWaitEvent(s_out, ev[1], 0)))
+    if (!cuda_ok(cudaEventRecord(ev[1], sl)) || !cuda_ok(cudaStreamWaitEvent(s_out, ev[1], 0)))
       break;
     cuda_ok(cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + off, od, bytes,
                             cudaMemcpyDeviceToHost, s_out));
@@ -232,6 +247,7 @@ extern "C" int cti_moe_layer_forward_host(
   // in flight).
   if (cudaEventRecord(ev[1], s_out) == cudaSuccess) cudaStreamWaitEvent(s, ev[1], 0);
   if (cudaEventRecord(ev[0], s_in) == cudaSuccess) cudaStreamWaitEvent(s, ev[0], 0);
+  if (two && cudaEventRecord(ev[0], s2) == cudaSuccess) cudaStreamWaitEvent(s, ev[0], 0);
   for (auto& e : ev) cudaEventDestroy(e);
   return rc;
 }

@@ -99,6 +99,10 @@ class TopKGate(nn.Module):
 class SMoE(nn.Module):
     """Top-2 sparse MoE layer: router -> dispatch -> grouped expert FFN -> combine."""
 
+    # forward_host's default chunk: measured on one B200 at cfg2 (72,214
+    # tokens, two compute streams), 4,096 tokens per chunk beat 2,048-9,027.
+    HOST_CHUNK_TOKENS = 4096
+
     def __init__(self, d_model: int, dim_ff: int, num_experts: int, k: int = 2,
                  activation: str = "gelu", renormalize: bool = True):
         super().__init__()
@@ -132,8 +136,10 @@ class SMoE(nn.Module):
         if not self._fused_ready or self._w1.device != device:
             self.prepare_for_inference()
 
-    def _get_workspace(self, T: int, device: torch.device) -> torch.Tensor:
+    def _get_workspace(self, T: int, device: torch.device, halves: int = 1) -> torch.Tensor:
         need = int(lib.cti_moe_layer_workspace_bytes(T, self.d_model, self.num_experts, self.dim_ff))
+        if halves == 2:  # two layers in flight: a 256-byte aligned first half, then the second
+            need += -(-need // 256) * 256
         ws = self._workspace
         if ws is None or ws.device != device or ws.numel() < need:
             ws = torch.empty(need, dtype=torch.uint8, device=device)
@@ -168,7 +174,8 @@ class SMoE(nn.Module):
         """``forward`` for activations in host memory: copies x to the GPU,
         runs the layer and copies the output back, pipelined over chunks of
         tokens (``cti_moe_layer_forward_host``) so that the two copies and
-        the layer overlap.  x_host [..., D] bf16 on the CPU (page-locked
+        the layer overlap; neighbouring chunks' layers run on two compute
+        streams, so that they overlap too.  x_host [..., D] bf16 on the CPU (page-locked
         for the overlap); returns ``(out_host, None)`` with out_host a
         page-locked CPU tensor of the same shape, valid once the current
         stream of ``device`` is synchronised.  The result equals
@@ -192,9 +199,10 @@ class SMoE(nn.Module):
         if T == 0:
             return out_host, None
         if chunk_tokens is None:
-            # Eight chunks balance the pipeline fill against the per-chunk
-            # launch cost; small layers run in one piece.
-            chunk_tokens = max(4096, -(-T // 8))
+            # Small chunks shorten the pipeline's fill and drain; with two
+            # layers in flight their fixed cost (~50 us per layer) stays
+            # below the copies' time.
+            chunk_tokens = self.HOST_CHUNK_TOKENS
         chunk = min(int(chunk_tokens), T)
         stage = getattr(self, "_host_stage", None)
         if stage is None or stage[0].device != dev or stage[0].numel() < T * D:
@@ -203,9 +211,10 @@ class SMoE(nn.Module):
             self._host_stage = stage
         streams = getattr(self, "_copy_streams", None)
         if streams is None or streams[0].device != dev:
-            streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+            streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
             self._copy_streams = streams
-        ws = self._get_workspace(chunk, dev)
+        two = T > chunk
+        ws = self._get_workspace(chunk, dev, halves=2 if two else 1)
         check(
             lib.cti_moe_layer_forward_host(
                 ptr(x_host), ptr(out_host), ptr(stage[0]), ptr(stage[1]), ptr(self._wg),
@@ -213,6 +222,7 @@ class SMoE(nn.Module):
                 self.num_experts, self.dim_ff, _lib.ACTIVATIONS[self.activation],
                 int(self.gate.renormalize), chunk, ptr(ws), ws.numel(), ptr(status_word(dev)),
                 stream_handle(dev), streams[0].cuda_stream, streams[1].cuda_stream,
+                streams[2].cuda_stream if two else None,
             ),
             "cti_moe_layer_forward_host",
         )

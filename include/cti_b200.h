@@ -240,17 +240,22 @@ int cti_moe_layer_forward(const void* x_bf16, const float* wg, const float* bg,
  * all T, bit for bit.
  *   x_host, out_host: [T,D] bf16 host memory (page-locked for the copies to
  *     run asynchronously); x_dev, out_dev: [T,D] bf16 device staging;
- *   workspace: cti_moe_layer_workspace_bytes(min(chunk_tokens, T), D, E, F).
+ *   workspace: W = cti_moe_layer_workspace_bytes(min(chunk_tokens, T), D, E,
+ *     F) bytes; with compute_stream2, W rounded up to 256 bytes plus W.
+ * compute_stream2 (may be NULL): odd chunks' layers run on it, on the second
+ * half of the workspace, so that the layers of neighbouring chunks overlap.
  * The copies start after the work enqueued on `stream` before the call, and
- * `stream` waits for the last copy back, so synchronising `stream` makes
- * out_host valid.  The copy streams may be `stream` itself (no overlap).
+ * `stream` waits for the last copy back (and for compute_stream2), so
+ * synchronising `stream` makes out_host valid.  The copy streams may be
+ * `stream` itself (no overlap).
  * ---------------------------------------------------------------------- */
 int cti_moe_layer_forward_host(const void* x_host, void* out_host, void* x_dev, void* out_dev,
                                const float* wg, const float* bg, const void* W1_bf16,
                                const float* b1, const void* W2_bf16, const float* b2, int64_t T,
                                int D, int E, int F, int act, int renorm, int64_t chunk_tokens,
                                void* workspace, size_t workspace_bytes, int32_t* status,
-                               void* stream, void* copy_stream_in, void* copy_stream_out);
+                               void* stream, void* copy_stream_in, void* copy_stream_out,
+                               void* compute_stream2);
 
 /* ------------------------------------------------------------------------
  * Stage 5 - 28-feature embedding-bag sum pooling.

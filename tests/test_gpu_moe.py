@@ -257,12 +257,13 @@ def test_layer_forward_host_c_abi_single_stream_and_errors(cuda_device):
                      device=cuda_device)
     s = stream_handle(cuda_device)
 
-    def call(xh=x_h, chunk_tokens=chunk, ws_bytes=None):
+    def call(xh=x_h, chunk_tokens=chunk, ws_bytes=None, s2=None, wsp=ws):
         return lib.cti_moe_layer_forward_host(
             ptr(xh) if xh is not None else None, ptr(out_h), ptr(xd), ptr(od), ptr(m._wg),
             ptr(m._bg), ptr(m._w1), ptr(m._b1), ptr(m._w2), ptr(m._b2), T, D, 16, 1024,
-            _lib.ACTIVATIONS["gelu"], 1, chunk_tokens, ptr(ws),
-            ws.numel() if ws_bytes is None else ws_bytes, ptr(status_word(cuda_device)), s, s, s)
+            _lib.ACTIVATIONS["gelu"], 1, chunk_tokens, ptr(wsp),
+            wsp.numel() if ws_bytes is None else ws_bytes, ptr(status_word(cuda_device)), s, s, s,
+            s2)
 
     assert call() == _lib.CTI_OK
     torch.cuda.current_stream(cuda_device).synchronize()
@@ -272,3 +273,13 @@ def test_layer_forward_host_c_abi_single_stream_and_errors(cuda_device):
     assert call(xh=None) == _lib.CTI_ERR_INVALID_ARG
     assert call(chunk_tokens=2048) == _lib.CTI_ERR_INVALID_ARG  # workspace sized for 1024
     assert call(ws_bytes=16) == _lib.CTI_ERR_INVALID_ARG
+    # A second compute stream: odd chunks on it, on the workspace's second half.
+    s2 = torch.cuda.Stream(cuda_device)
+    assert call(s2=s2.cuda_stream) == _lib.CTI_ERR_INVALID_ARG  # one half only
+    half = -(-ws.numel() // 256) * 256
+    ws2 = torch.empty(half + ws.numel(), dtype=torch.uint8, device=cuda_device)
+    out_h.zero_()
+    assert call(s2=s2.cuda_stream, wsp=ws2) == _lib.CTI_OK
+    torch.cuda.current_stream(cuda_device).synchronize()
+    _lib.raise_on_status(cuda_device)
+    assert torch.equal(out_h, ref)
