@@ -144,19 +144,34 @@ CTI_DEVICE void block_chunks(int st0, int tlast, int kb, int& cmin, int& cmax) {
   cmax = (min(tlast, kb + kKB - 1) - kb) >> 5;
 }
 
-// Writes row t's output (head h): o (32 fp32 TMEM columns) / l as bf16.
-CTI_DEVICE void store_row(__nv_bfloat16* __restrict__ out, int t, int H, int h,
-                          const uint32_t (&o)[32], float l) {
+// Writes the output rows of a warp's 32 lanes (head h): lane i's row t (or
+// -1: none) is o (32 fp32 TMEM columns) / l as bf16, 64 bytes.  Lanes 2j and
+// 2j+1 swap 32-byte halves first, so that each store writes one whole row
+// piece with two lanes instead of every lane writing half of its own.
+CTI_DEVICE void store_rows(__nv_bfloat16* __restrict__ out, int t, int H, int h,
+                           const uint32_t (&o)[32], float l, int lane, bool aligned32) {
   const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-  uint4* dst = reinterpret_cast<uint4*>(out + ((int64_t)t * H + h) * kHD);
+  uint32_t u[2][8];  // half j, word w: columns 16j + 2w, 16j + 2w + 1
 #pragma unroll
-  for (int q = 0; q < kHD / 8; ++q) {
-    uint4 w;
-    w.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
-    w.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
-    w.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
-    w.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
-    dst[q] = w;
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+      u[j][w] = pack_bf16x2(__uint_as_float(o[16 * j + 2 * w]) * inv,
+                            __uint_as_float(o[16 * j + 2 * w + 1]) * inv);
+  const bool odd = (lane & 1) != 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? u[0][w] : u[1][w], 1);
+    if (odd)
+      u[0][w] = got;
+    else
+      u[1][w] = got;
+  }
+  // Now slot k holds half (lane & 1) of the row of lane (lane & ~1) + k.
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int tk = __shfl_sync(0xffffffffu, t, (lane & ~1) + k);
+    if (tk >= 0) st_global_32B(out + ((int64_t)tk * H + h) * kHD + 16 * (lane & 1), u[k], aligned32);
   }
 }
 
@@ -407,6 +422,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const uint32_t lane_base = tmem_base + ((uint32_t)(wq * 32) << 16);
     const float kNegInf = -INFINITY;
     const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    const bool out32 = (reinterpret_cast<uintptr_t>(out) & 31) == 0;
     // The previous tile's row, finished once its last PV MMA is done.
     int prev_t = -1, prev_h = 0, prev_o = 0, prev_g = -1;
     float prev_l = 0.0f;
@@ -421,18 +437,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     };
     auto finish_prev = [&]() -> bool {
       if (prev_g < 0) return true;
-      if (!wait_pv(prev_g, 0x60d)) return false;
+      // Warp-uniform: the TMEM load and the row exchange below need every lane.
+      if (!__all_sync(0xffffffffu, wait_pv(prev_g, 0x60d))) return false;
       tc_fence_after();
       uint32_t o[32];
       tmem_ld_32x32b_x32_sync(lane_base + kOCol0 + (uint32_t)prev_o * kHD, o);
-      if (prev_t >= 0) store_row(out, prev_t, H, prev_h, o, prev_l);
+      store_rows(out, prev_t, H, prev_h, o, prev_l, lane, out32);
       prev_g = -1;
       return true;
     };
     for (int64_t i = blockIdx.x; ok && i < ntiles; i += gridDim.x, ++it) {
       const int si = it % kInfoSlots;
-      if (!mbar_wait(&info_full[si], (uint32_t)((it / kInfoSlots) & 1), status, 0x60c,
-                     abort_flag))
+      if (!__all_sync(0xffffffffu, mbar_wait(&info_full[si], (uint32_t)((it / kInfoSlots) & 1),
+                                             status, 0x60c, abort_flag)))
         break;
       const int t0 = slots[si].t0, h = slots[si].h, st0 = slots[si].st0;
       const int tlast = slots[si].tlast, kbtop = slots[si].kbtop, nkb = slots[si].nkb;
@@ -464,7 +481,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const int whi = __reduce_max_sync(0xffffffffu, hi);
         const int c_lo = whi >= 0 ? (wlo >> 5) : 2;
         const int c_hi = whi >= 0 ? (whi >> 5) : -1;
-        if (!mbar_wait(&s_full[b], (uint32_t)((g / kNS) & 1), status, 0x60e, abort_flag)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)((g / kNS) & 1), status,
+                                               0x60e, abort_flag))) {
           ok = false;
           break;
         }
@@ -509,7 +527,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         }
         if (__any_sync(0xffffffffu, corr != 1.0f)) {
           // O holds blocks up to g-1 of this tile: wait for PV_{g-1}.
-          if (!wait_pv(g - 1, 0x60f)) {
+          if (!__all_sync(0xffffffffu, wait_pv(g - 1, 0x60f))) {
             ok = false;
             break;
           }
