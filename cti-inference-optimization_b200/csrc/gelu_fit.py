@@ -8,9 +8,10 @@ erfc(|x|/sqrt2)/2 for x < 0.  With u = |x| and h(u) = erfc(u/sqrt2)/2,
 where P(u) = log2(erfc(u/sqrt2)/2) = log2(erfcx(u/sqrt2)) - u^2 log2(e)/2 - 1
 is smooth (the -u^2 decay is exactly a polynomial term).  P is approximated
 on [0, U0] by a Chebyshev least-squares fit of degree DEG, converted to
-monomial coefficients for Horner evaluation in fp32; the kernel clamps u to
-U0 = 6 before the polynomial, where h(6) = 9.9e-10, so past it GELU(x) is
-max(x, 0) - |x| * 9.9e-10: an absolute error below 1.2e-8 for |x| <= 12.
+monomial coefficients for Horner evaluation in fp32.  The kernel does not
+clamp u: past U0 = 6 the polynomial keeps falling (P(6) = -29.9 is its
+largest value there), so h stays below h(6) = 9.9e-10 and goes to 0, and
+GELU(x) is within |x| * 9.9e-10 of max(x, 0).
 
 Run:  python csrc/gelu_fit.py   (prints the coefficient table and the
 fp32-simulated error of GELU against the exact function).
@@ -37,10 +38,10 @@ def fit():
 
 def gelu_fp32(x, coef):
     """fp32 simulation of the kernel's evaluation order (gelu.cuh): Horner
-    on the clamped |x|, then GELU(x) = max(x, 0) - |x| * 2^P."""
+    on |x|, then GELU(x) = max(x, 0) - |x| * 2^P."""
     x = x.astype(np.float32)
     u = np.abs(x)
-    uc = np.minimum(u, np.float32(U0))
+    uc = u  # no clamp (see the module docstring)
     acc = np.full_like(x, coef[-1])
     for ck in coef[-2::-1]:
         acc = (acc * uc + ck).astype(np.float32)
