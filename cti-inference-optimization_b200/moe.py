@@ -170,7 +170,8 @@ class SMoE(nn.Module):
 
     @torch.no_grad()
     def forward_host(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None,
-                     chunk_tokens: int | None = None, device: torch.device | None = None):
+                     chunk_tokens: int | None = None, device: torch.device | None = None,
+                     graph: bool = False):
         """``forward`` for activations in host memory: copies x to the GPU,
         runs the layer and copies the output back, pipelined over chunks of
         tokens (``cti_moe_layer_forward_host``) so that the two copies and
@@ -179,7 +180,13 @@ class SMoE(nn.Module):
         for the overlap); returns ``(out_host, None)`` with out_host a
         page-locked CPU tensor of the same shape, valid once the current
         stream of ``device`` is synchronised.  The result equals
-        ``forward`` on the same rows bit for bit."""
+        ``forward`` on the same rows bit for bit.
+
+        ``graph=True`` (page-locked x_host and out_host): the first call with
+        a given pair of buffers runs the pipeline and captures it in a CUDA
+        graph; later calls with the same buffers (whatever their contents)
+        and shapes replay it, without the host launching each chunk's copies
+        and kernels again."""
         if x_host.is_cuda or x_host.dtype != torch.bfloat16 or x_host.shape[-1] != self.d_model:
             raise ValueError("x_host must be a CPU bf16 tensor [..., d_model]")
         if not x_host.is_contiguous():
@@ -215,17 +222,42 @@ class SMoE(nn.Module):
             self._copy_streams = streams
         two = T > chunk
         ws = self._get_workspace(chunk, dev, halves=2 if two else 1)
-        check(
-            lib.cti_moe_layer_forward_host(
-                ptr(x_host), ptr(out_host), ptr(stage[0]), ptr(stage[1]), ptr(self._wg),
-                ptr(self._bg), ptr(self._w1), ptr(self._b1), ptr(self._w2), ptr(self._b2), T, D,
-                self.num_experts, self.dim_ff, _lib.ACTIVATIONS[self.activation],
-                int(self.gate.renormalize), chunk, ptr(ws), ws.numel(), ptr(status_word(dev)),
-                stream_handle(dev), streams[0].cuda_stream, streams[1].cuda_stream,
-                streams[2].cuda_stream if two else None,
-            ),
-            "cti_moe_layer_forward_host",
-        )
+        status = status_word(dev)
+
+        def launch():
+            check(
+                lib.cti_moe_layer_forward_host(
+                    ptr(x_host), ptr(out_host), ptr(stage[0]), ptr(stage[1]), ptr(self._wg),
+                    ptr(self._bg), ptr(self._w1), ptr(self._b1), ptr(self._w2), ptr(self._b2),
+                    T, D, self.num_experts, self.dim_ff, _lib.ACTIVATIONS[self.activation],
+                    int(self.gate.renormalize), chunk, ptr(ws), ws.numel(), ptr(status),
+                    stream_handle(dev), streams[0].cuda_stream, streams[1].cuda_stream,
+                    streams[2].cuda_stream if two else None,
+                ),
+                "cti_moe_layer_forward_host",
+            )
+
+        if not graph:
+            launch()
+            return out_host, None
+        if not (x_host.is_pinned() and out_host.is_pinned()):
+            raise ValueError("graph=True needs page-locked x_host and out_host")
+        key = (dev.index, T, chunk, ptr(x_host), ptr(out_host), ptr(stage[0]), ptr(stage[1]),
+               ptr(ws), ptr(status), ptr(self._wg), ptr(self._w1), ptr(self._w2))
+        graphs = getattr(self, "_host_graphs", None)
+        if graphs is None:
+            graphs = self._host_graphs = {}
+        g = graphs.get(key)
+        if g is not None:
+            g.replay()
+            return out_host, None
+        launch()  # this call's result; also sets up every kernel before the capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch()
+        if len(graphs) >= 4:  # keep the few most recent buffer pairs
+            graphs.pop(next(iter(graphs)))
+        graphs[key] = g
         return out_host, None
 
     @torch.no_grad()

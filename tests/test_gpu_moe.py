@@ -238,6 +238,30 @@ def test_forward_host_reuses_buffers_and_orders_after_prior_work(cuda_device):
     _lib.raise_on_status(cuda_device)
 
 
+def test_forward_host_graph_replays_with_new_contents(cuda_device):
+    """forward_host(graph=True): the first call runs and captures the
+    pipeline, later calls replay it; new contents written into the same
+    page-locked input buffer give their own outputs, bit for bit equal to the
+    device forward."""
+    from cti_b200 import _lib, synth
+
+    m = _cfg2_module(cuda_device, seed=3)
+    T = 30000
+    x_h = torch.empty(T, 256, dtype=torch.bfloat16).pin_memory()
+    out_h = torch.empty(T, 256, dtype=torch.bfloat16).pin_memory()
+    for s in (7, 8, 9):
+        x = synth.moe_activations(T, 256, seed=s)
+        ref = m(x.to(cuda_device).unsqueeze(0))[0][0].cpu()
+        x_h.copy_(x)
+        out_h.zero_()
+        m.forward_host(x_h, out_h, chunk_tokens=4096, graph=True)
+        torch.cuda.current_stream(cuda_device).synchronize()
+        assert torch.equal(out_h, ref), s
+    _lib.raise_on_status(cuda_device)
+    with pytest.raises(ValueError):
+        m.forward_host(x_h.clone(), graph=True)  # pageable input
+
+
 def test_layer_forward_host_c_abi_single_stream_and_errors(cuda_device):
     """The C entry point with the copy streams equal to the compute stream,
     and its argument checks."""
