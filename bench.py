@@ -260,6 +260,39 @@ def cpu_baseline_moe(cfg, seconds: float, sample_tokens: int | None = CPU_SAMPLE
                       f"({el:.1f} s), fp32, oracle/moe_ref.py (baseline/infer.py:280-358)"}
 
 
+def cpu_baseline_embbag(bb, table_dev, seconds: float, sample_bags: int = 1024) -> dict:
+    """The oracle port of the reference pooling (baseline/infer.py:253-263:
+    per slot, emb(values.clamp) then segment_reduce(sum), fp32) on all host
+    cores over the first `sample_bags` samples of the batch (all 28
+    features), repeated for about `seconds`; GB/s of the sample's algorithmic
+    bytes, counted as for the GPU line."""
+    from oracle import embbag_ref as er
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    F_, B = bb.features, bb.batch
+    S = min(sample_bags, B)
+    ro = bb.row_offsets.view(F_, B + 1)
+    sub_ro = ro[:, :S + 1].contiguous()
+    n_ids = int((sub_ro[:, -1] - sub_ro[:, 0]).sum())
+    table = table_dev.cpu()
+    args = (bb.values, sub_ro.view(-1), bb.val_offsets, table, bb.table_row_base, bb.vocab, F_)
+    byts = 8 * n_ids + 8 * F_ * (S + 1) + 128 * n_ids + 4 * S * F_ * 64
+    er.embbag_ref(*args)  # warm-up
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        er.embbag_ref(*args)
+        n += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and n >= 2) or n >= 10000:
+            break
+    return {"value": n * byts / el / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "config": "cfg3",
+            "sample": f"the first {S} of {B} samples, all {F_} features ({n_ids} ids) per call, "
+                      f"{n} calls ({el:.1f} s), fp32, oracle/embbag_ref.py "
+                      f"(baseline/infer.py:253-263)"}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's CPU expert loop (the oracle port of
     baseline/infer.py:280-358, fp32, all host cores) over the whole
@@ -1077,6 +1110,9 @@ def run_embbag(args, world, rank, local):
     peaks, src = load_peaks()
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_embbag(bb, table, min(args.cpu_seconds, 15.0))
     line = {
         "metric": "embedding_bag_GBps", "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
@@ -1100,6 +1136,7 @@ def run_embbag(args, world, rank, local):
                              "kernel is bound by its dependent gathers, not by HBM"},
         "gpu_launches": args.steps,
         "clocks": clocks,
+        "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
 

@@ -25,13 +25,15 @@
 // their ring until the epilogue has written the matching H slab, and with
 // one ring for both they held the slots GEMM1(c+1)'s slabs needed.  The
 // even CTA (leader) issues every MMA; the barriers it waits on live in its
-// shared memory - the peer's TMA loads complete on them (.cta_group::2) and
-// the peer's epilogue warps arrive on them through shared::cluster
-// addresses; MMA completions that both CTAs wait for are committed twice,
-// once to each CTA's copy of the barrier.
+// shared memory - the peer's TMA loads complete on them (.cta_group::2), and
+// the peer's epilogue arrivals reach them through one forwarding thread of
+// the peer (a cluster-scope arrival per completed phase, warp 1 lane 0); MMA
+// completions that both CTAs wait for are committed twice, once to each
+// CTA's copy of the barrier.
 //
 // Roles per CTA (608 threads): warp 0 TMA producer of X and W1, warp 1 TMEM
-// allocation for the pair and (leader) MMA issuer, warp 2 TMA producer of
+// allocation for the pair and the MMA issuer (leader) or the forwarding
+// thread (peer), warp 2 TMA producer of
 // W2, warps 3-18 epilogue.  Epilogue warp (lane quadrant q, group s) owns
 // rows 32q..32q+31 and, of every 64-wide K slab, columns [16s, 16s + 16).
 // Biases are read through the read-only cache, one slab ahead.  The output
