@@ -15,6 +15,8 @@ e2e    the same through the public API with host buffers
        the copies of one token chunk overlap the layer on its neighbours.
 roofline  the dominant kernel (the expert FFN GEMM) timed alone with CUDA
        events: algorithmic FLOPs / mean launch time vs the measured bf16 peak.
+router_fp32  the router's exact fp32 logits against the nominal fp32 FMA
+       rate (its roofline: the FMA pipe, not HBM).
 cpu_baseline  the reference's PyTorch CPU expert loop (oracle port of
        baseline/infer.py:280-358, fp32) on a bounded token sample, rank 0,
        N=1 only; cpu_baseline_cfg1 the same loop at configuration 1.
@@ -69,6 +71,9 @@ def load_peaks():
         d = json.loads(p.read_text())
         return d, "measured"
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 74.4
 
 
 def ncu_traffic(kernel_key: str):
@@ -540,6 +545,16 @@ def run_ours(args, world, rank, local):
         "stages_ms": stages,
         "stages_hbm": stage_bandwidths(stages, T, cfg.d_model, cfg.num_experts,
                                        float(peaks["hbm_gbs"])),
+        # The router's exact fp32 logits run on the FMA pipe: T*E*D FMAs
+        # against the nominal fp32 rate (148 SMs x 128 lanes x 2 FLOP at
+        # 1.965 GHz), which alone needs 69 % of its HBM time at cfg2.
+        "router_fp32": {"flops": 2.0 * T * cfg.num_experts * cfg.d_model,
+                        "tflops": 2.0 * T * cfg.num_experts * cfg.d_model
+                        / (stages["router"] / 1e3) / 1e12,
+                        "peak_tflops": FP32_NOMINAL_TFLOPS,
+                        "frac": 2.0 * T * cfg.num_experts * cfg.d_model
+                        / (stages["router"] / 1e3) / 1e12 / FP32_NOMINAL_TFLOPS,
+                        "peak_source": "nominal (148 SMs x 128 FP32 lanes x 2 FLOP x 1.965 GHz)"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
