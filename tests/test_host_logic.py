@@ -152,3 +152,20 @@ def test_sequence_subbatch_pools_like_the_whole_batch():
                         table, bb.table_row_base, bb.vocab, bb.features)
     rows = torch.cat([torch.arange(int(uo[s]), int(uo[s + 1])) for s in seqs])
     assert torch.equal(pooled, full[rows])
+
+
+def test_host_pipeline_workspace_halves_match_the_c_requirement():
+    """forward_host with two compute streams needs the workspace of one chunk
+    rounded up to 256 bytes plus that of a second chunk (the C entry point's
+    check, include/cti_b200.h); SMoE._get_workspace(halves=2) sizes it so."""
+    from cti_b200._lib import lib
+
+    m = cti_b200.SMoE(256, 1024, 16)
+    for chunk in (1, 1000, 4096, 9027):
+        need = int(lib.cti_moe_layer_workspace_bytes(chunk, 256, 16, 1024))
+        m._workspace = None
+        one = m._get_workspace(chunk, torch.device("cpu"))
+        m._workspace = None
+        two = m._get_workspace(chunk, torch.device("cpu"), halves=2)
+        assert one.numel() == need
+        assert two.numel() == -(-need // 256) * 256 + need
